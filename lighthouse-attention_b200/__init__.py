@@ -1,0 +1,17 @@
+"""lighthouse_b200 — B200 (sm_100a) implementation of Lighthouse selection attention.
+
+The directory is named ``lighthouse-attention_b200``; it is imported under the
+package name ``lighthouse_b200`` (see ``load_package`` in __graft_entry__.py
+or INTEGRATION.md).  Modules:
+
+  lighthouse_selection       drop-in for the reference module of the same name
+  lighthouse_selection_cuda  drop-in for the reference module of the same name
+  cp                         context-parallel layer (NCCL all-gather of selected K/V)
+  _native                    ctypes binding of liblighthouse_b200.so (include/lighthouse_b200.h)
+"""
+from . import _native  # noqa: F401
+from .lighthouse_selection import (DialatedLighthouseNormScorer, DialatedLighthouseNormScorerCP,  # noqa: F401
+                                   DilatedLighthouseGLAScorer, DilatedLighthouseScorer, LighthouseCP,
+                                   LighthouseLocal, compute_output_indices_selection, lighthouse_attention,
+                                   scatter_to_base_sequence)
+from .lighthouse_selection_cuda import LighthouseSelectionQkKqChunkedTopkNvrtc  # noqa: F401

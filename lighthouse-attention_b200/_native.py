@@ -1,0 +1,229 @@
+"""ctypes binding of liblighthouse_b200.so (the C ABI in include/lighthouse_b200.h).
+
+Every wrapper takes torch CUDA tensors, checks dtype / layout / device,
+allocates outputs with torch's caching allocator on the input's device and
+enqueues the kernels on ``torch.cuda.current_stream()``.  There is no CPU or
+eager-PyTorch fallback: if the library is missing or the device is not a
+B200 the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+
+import torch
+
+_LIB_PATH = pathlib.Path(__file__).resolve().parent / "liblighthouse_b200.so"
+_lib = None
+
+LH_DTYPE = {torch.bfloat16: 0, torch.float32: 1}
+_VP = ctypes.c_void_p
+
+
+class LighthouseError(RuntimeError):
+    """Raised when a C-ABI entry point returns a non-zero status."""
+
+
+class LighthouseShapeError(ValueError):
+    """The C ABI rejected a shape (LH_ERR_SHAPE)."""
+
+
+_SIGS = {
+    "lh_last_error": (ctypes.c_char_p, []),
+    "lh_abi_version": (ctypes.c_int, []),
+    "lh_device_status": (ctypes.c_int, [ctypes.c_int]),
+    "lh_pyramid_score_fwd": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int] + [ctypes.c_int] * 6 + [_VP] * 6),
+    "lh_select_topk": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 6 + [_VP, _VP, _VP]),
+    "lh_build_inverse": (ctypes.c_int, [_VP] + [ctypes.c_int] * 4 + [_VP, _VP]),
+    "lh_gather_selected": (ctypes.c_int, [_VP] * 6 + [ctypes.c_int] * 6 + [_VP, ctypes.c_int] + [_VP] * 4),
+    "lh_attn_fwd": (ctypes.c_int, [_VP] * 3 + [ctypes.c_int] * 6 + [ctypes.c_float, _VP, _VP, _VP]),
+    "lh_attn_bwd_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 5),
+    "lh_attn_bwd": (ctypes.c_int, [_VP] * 6 + [ctypes.c_int] * 6 + [ctypes.c_float] + [_VP] * 4
+                    + [ctypes.c_size_t, _VP]),
+    "lh_scatter_fwd": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
+    "lh_scatter_bwd": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
+    "lh_unpool_bwd": (ctypes.c_int, [_VP] * 4 + [ctypes.c_int] * 8 + [_VP] * 4),
+}
+
+
+def lib_path() -> pathlib.Path:
+    return _LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            raise ImportError(
+                f"{_LIB_PATH} is not built; run `python lighthouse-attention_b200/build.py` "
+                "(the CUDA path has no fallback)")
+        lib = ctypes.CDLL(str(_LIB_PATH))
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        msg = load().lh_last_error().decode(errors="replace")
+        if rc == 1:
+            raise LighthouseShapeError(msg)
+        raise LighthouseError(f"lighthouse_b200 error {rc}: {msg}")
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("lighthouse_b200 ops take CUDA tensors (no CPU path)")
+
+
+def device_status(reset: bool = True) -> int:
+    return load().lh_device_status(1 if reset else 0)
+
+
+# --------------------------------------------------------------------------- geometry
+def pyramid_len(N: int, L: int, p: int) -> int:
+    return sum(N // p ** l for l in range(L))
+
+
+def sel_len(N: int, L: int, p: int, k: int) -> int:
+    return N // p ** (L - 1) + (L - 1) * p * k
+
+
+# --------------------------------------------------------------------------- ops
+def pyramid_score(xq, xk, xv, L: int, p: int):
+    """(B,S,H,D) x3 -> pooled q/k/v (B,H,S_pool,D), scores_qk/kq (B,H,S_tot) fp32."""
+    _require_cuda(xq, xk, xv)
+    xq, xk, xv = xq.contiguous(), xk.contiguous(), xv.contiguous()
+    B, S, H, D = xq.shape
+    S_tot = pyramid_len(S, L, p)
+    S_pool = S_tot - S
+    pq = torch.empty(B, H, S_pool, D, dtype=xq.dtype, device=xq.device)
+    pk, pv = torch.empty_like(pq), torch.empty_like(pq)
+    sqk = torch.empty(B, H, S_tot, dtype=torch.float32, device=xq.device)
+    skq = torch.empty_like(sqk)
+    _check(load().lh_pyramid_score_fwd(_ptr(xq), _ptr(xk), _ptr(xv), LH_DTYPE[xq.dtype], B, S, H, D, L, p,
+                                       _ptr(pq), _ptr(pk), _ptr(pv), _ptr(sqk), _ptr(skq), _stream()))
+    return pq, pk, pv, sqk, skq
+
+
+def select_topk(scores_qk, scores_kq, L: int, p: int, k: int, N: int, with_inverse: bool = True):
+    """Selection indices (B,H,S_sel) int32 and inverse map (B,H,S_tot) int32."""
+    _require_cuda(scores_qk, scores_kq)
+    if scores_qk.shape != scores_kq.shape:
+        raise AssertionError("scores_qk and scores_kq must have the same shape")
+    sq = scores_qk.float().contiguous()
+    sk = scores_kq.float().contiguous()
+    B, H, S_tot = sq.shape
+    if S_tot != pyramid_len(N, L, p):
+        raise LighthouseShapeError(f"scores length {S_tot} != pyramid length {pyramid_len(N, L, p)}")
+    S_sel = sel_len(N, L, p, k)
+    idx = torch.empty(B, H, S_sel, dtype=torch.int32, device=sq.device)
+    inv = torch.empty(B, H, S_tot, dtype=torch.int32, device=sq.device) if with_inverse else None
+    _check(load().lh_select_topk(_ptr(sq), _ptr(sk), B, H, N, L, p, k, _ptr(idx), _ptr(inv), _stream()))
+    return idx, inv
+
+
+def build_inverse(indices, S_tot: int):
+    _require_cuda(indices)
+    indices = indices.to(torch.int32).contiguous()
+    B, H, S_sel = indices.shape
+    inv = torch.empty(B, H, S_tot, dtype=torch.int32, device=indices.device)
+    _check(load().lh_build_inverse(_ptr(indices), B, H, S_sel, S_tot, _ptr(inv), _stream()))
+    return inv
+
+
+def gather_selected(raws, pooleds, indices):
+    """raws: 3 tensors (B,S,H,D) (or None); pooleds: 3 tensors (B,H,S_pool,D)."""
+    first = next(r for r in raws if r is not None)
+    B, S, H, D = first.shape
+    S_pool = next(p for p in pooleds if p is not None).shape[2]
+    S_sel = indices.shape[-1]
+    outs = [None if r is None else torch.empty(B, H, S_sel, D, dtype=r.dtype, device=r.device) for r in raws]
+    raws = [None if r is None else r.contiguous() for r in raws]
+    pooleds = [None if p is None else p.contiguous() for p in pooleds]
+    _check(load().lh_gather_selected(*[_ptr(r) for r in raws], *[_ptr(p) for p in pooleds],
+                                     LH_DTYPE[first.dtype], B, S, H, D, S_pool, _ptr(indices), S_sel,
+                                     *[_ptr(o) for o in outs], _stream()))
+    return outs
+
+
+def _attn_operands(*ts):
+    _require_cuda(*ts)
+    for t in ts:
+        if t.dtype != torch.bfloat16 or t.shape[-1] != 128:
+            raise ValueError("attention kernels take bf16 tensors with head dim 128")
+    return [t.contiguous() for t in ts]
+
+
+def attn_fwd(q, k, v, scale: float, q_off: int = 0):
+    """Causal attention; query row r at position q_off + r, key row c at c."""
+    q, k, v = _attn_operands(q, k, v)
+    B, H, S_q, D = q.shape
+    S_kv = k.shape[2]
+    o = torch.empty_like(q)
+    lse = torch.empty(B, H, S_q, dtype=torch.float32, device=q.device)
+    _check(load().lh_attn_fwd(_ptr(q), _ptr(k), _ptr(v), B, H, S_q, S_kv, q_off, D, scale, _ptr(o), _ptr(lse),
+                              _stream()))
+    return o, lse
+
+
+def attn_bwd_workspace_size(B: int, H: int, S_q: int, S_kv: int, D: int) -> int:
+    return int(load().lh_attn_bwd_workspace_size(B, H, S_q, S_kv, D))
+
+
+def attn_bwd(q, k, v, o, lse, do, scale: float, q_off: int = 0):
+    q, k, v, o, do = _attn_operands(q, k, v, o, do)
+    B, H, S_q, D = q.shape
+    S_kv = k.shape[2]
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ws_bytes = attn_bwd_workspace_size(B, H, S_q, S_kv, D)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    _check(load().lh_attn_bwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse.contiguous()), _ptr(do), B, H, S_q,
+                              S_kv, q_off, D, scale, _ptr(dq), _ptr(dk), _ptr(dv), _ptr(ws), ws_bytes, _stream()))
+    return dq, dk, dv
+
+
+def scatter_fwd(attn, inverse, N_shard: int, N_total: int, L: int, p: int):
+    attn = attn.contiguous()
+    B, H, S_sel, D = attn.shape
+    out = torch.empty(B, H, N_total, D, dtype=attn.dtype, device=attn.device)
+    _check(load().lh_scatter_fwd(_ptr(attn), _ptr(inverse), LH_DTYPE[attn.dtype], B, H, S_sel, D, N_shard, N_total,
+                                 L, p, _ptr(out), _stream()))
+    return out
+
+
+def scatter_bwd(dout, indices, N_shard: int, N_total: int, L: int, p: int):
+    dout = dout.contiguous()
+    B, H, _, D = dout.shape
+    S_sel = indices.shape[-1]
+    dattn = torch.empty(B, H, S_sel, D, dtype=dout.dtype, device=dout.device)
+    _check(load().lh_scatter_bwd(_ptr(dout), _ptr(indices), LH_DTYPE[dout.dtype], B, H, S_sel, D, N_shard,
+                                 N_total, L, p, _ptr(dattn), _stream()))
+    return dattn
+
+
+def unpool_bwd(dsels, inverse, S: int, L: int, p: int):
+    first = next(d for d in dsels if d is not None)
+    B, H, S_sel, D = first.shape
+    dsels = [None if d is None else d.contiguous() for d in dsels]
+    outs = [None if d is None else torch.empty(B, S, H, D, dtype=d.dtype, device=d.device) for d in dsels]
+    _check(load().lh_unpool_bwd(*[_ptr(d) for d in dsels], _ptr(inverse), LH_DTYPE[first.dtype], B, S, H, D, L, p,
+                                S_sel, *[_ptr(o) for o in outs], _stream()))
+    return outs

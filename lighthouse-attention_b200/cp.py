@@ -1,0 +1,151 @@
+"""Context-parallel Lighthouse layer (LighthouseCP, reference src/lighthouse_selection.py:985-1054).
+
+Sharding (head/tail load balance, as torch's context_parallel load balancer
+does for the reference): the global sequence is cut into 2W equal chunks and
+rank r holds chunks r and 2W-1-r, concatenated, as its local shard.
+
+Per rank:
+  1. each local half is pooled, scored and selected on its own with
+     k / (2W) (pooling restarts per chunk: SEL:1014-1029);
+  2. the selected K and V of both halves are all-gathered over the CP group
+     (one NCCL all_gather) and laid out in global chunk order;
+  3. the selected queries of chunk c attend causally to the selections of
+     chunks 0..c (query row r of chunk c sits at global selected position
+     c * S_c + r) -- the same result torch's ring attention gives the
+     reference under context_parallel;
+  4. each half's output is scattered back into its half (SEL:1046-1054).
+Backward: dQ stays local; dK/dV partials for every chunk are summed over
+ranks with one reduce-scatter (fp32) so each rank receives its own chunks'.
+
+``ops`` is the kernel namespace (``_native`` on the GPU); tests may pass a
+namespace with the same functions to exercise the host logic on CPU ranks.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from . import _native
+
+
+def _owner(c: int, W: int) -> tuple[int, int]:
+    """(rank, slot) holding global chunk c: slot 0 = head half, 1 = tail half."""
+    return (c, 0) if c < W else (2 * W - 1 - c, 1)
+
+
+def _all_gather(t: torch.Tensor, W: int, group):
+    if W == 1:
+        return [t]
+    outs = [torch.empty_like(t) for _ in range(W)]
+    dist.all_gather(outs, t.contiguous(), group=group)
+    return outs
+
+
+def _reduce_scatter(t: torch.Tensor, W: int, group) -> torch.Tensor:
+    """t: (W, ...) rank-ordered blocks; returns this rank's summed block."""
+    if W == 1:
+        return t[0]
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty_like(t[0])
+        dist.reduce_scatter_tensor(out, t.contiguous(), group=group)
+        return out
+    dist.all_reduce(t, group=group)          # gloo (CPU test ranks) has no reduce-scatter
+    return t[dist.get_rank(group)].clone()
+
+
+class _SelectHalfFn(torch.autograd.Function):
+    """Pyramid + selection + gather of one chunk; backward = un-pool."""
+
+    @staticmethod
+    def forward(ctx, xq, xk, xv, L, p, k, ops):
+        B, S, H, D = xq.shape
+        pq, pk, pv, sqk, skq = ops.pyramid_score(xq, xk, xv, L, p)
+        idx, inv = ops.select_topk(sqk, skq, L, p, k, S)
+        qs, ks, vs = ops.gather_selected([xq, xk, xv], [pq, pk, pv], idx)
+        ctx.save_for_backward(inv)
+        ctx.args = (S, L, p, ops)
+        ctx.mark_non_differentiable(idx, inv)
+        return qs, ks, vs, idx, inv
+
+    @staticmethod
+    def backward(ctx, dqs, dks, dvs, _di, _dv):
+        (inv,) = ctx.saved_tensors
+        S, L, p, ops = ctx.args
+        dxq, dxk, dxv = ops.unpool_bwd([dqs, dks, dvs], inv, S, L, p)
+        return dxq, dxk, dxv, None, None, None, None
+
+
+class _ScatterInvFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, attn, idx, inv, N, L, p, ops):
+        ctx.save_for_backward(idx)
+        ctx.args = (N, L, p, ops)
+        return ops.scatter_fwd(attn, inv, N, N, L, p)
+
+    @staticmethod
+    def backward(ctx, dout):
+        (idx,) = ctx.saved_tensors
+        N, L, p, ops = ctx.args
+        return ops.scatter_bwd(dout, idx, N, N, L, p), None, None, None, None, None, None
+
+
+class _CPAttentionFn(torch.autograd.Function):
+    """Causal attention of the two local query chunks against all ranks' K/V."""
+
+    @staticmethod
+    def forward(ctx, qh, qt, kh, kt, vh, vt, rank, W, group, ops):
+        B, H, S_c, D = qh.shape
+        kv = torch.stack([kh, kt, vh, vt])                    # (4, B, H, S_c, D)
+        gathered = _all_gather(kv, W, group)                  # rank order
+        chunks_k, chunks_v = [], []
+        for c in range(2 * W):
+            r, slot = _owner(c, W)
+            chunks_k.append(gathered[r][slot])
+            chunks_v.append(gathered[r][2 + slot])
+        K = torch.cat(chunks_k, dim=2).contiguous()           # global chunk order
+        V = torch.cat(chunks_v, dim=2).contiguous()
+        scale = 1.0 / math.sqrt(D)
+        a, b = rank, 2 * W - 1 - rank
+        oh, lh = ops.attn_fwd(qh, K, V, scale, q_off=a * S_c)
+        ot, lt = ops.attn_fwd(qt, K, V, scale, q_off=b * S_c)
+        ctx.save_for_backward(qh, qt, K, V, oh, ot, lh, lt)
+        ctx.args = (rank, W, group, ops, scale, S_c)
+        return oh, ot
+
+    @staticmethod
+    def backward(ctx, doh, dot):
+        qh, qt, K, V, oh, ot, lh, lt = ctx.saved_tensors
+        rank, W, group, ops, scale, S_c = ctx.args
+        a, b = rank, 2 * W - 1 - rank
+        dqh, dKh, dVh = ops.attn_bwd(qh, K, V, oh, lh, doh, scale, q_off=a * S_c)
+        dqt, dKt, dVt = ops.attn_bwd(qt, K, V, ot, lt, dot, scale, q_off=b * S_c)
+        dK = dKh.float() + dKt.float()                        # (B, H, 2W*S_c, D), global chunk order
+        dV = dVh.float() + dVt.float()
+        B, H, _, D = dK.shape
+        blocks = torch.empty(W, 4, B, H, S_c, D, dtype=torch.float32, device=dK.device)
+        for c in range(2 * W):
+            r, slot = _owner(c, W)
+            blocks[r, slot] = dK[:, :, c * S_c:(c + 1) * S_c]
+            blocks[r, 2 + slot] = dV[:, :, c * S_c:(c + 1) * S_c]
+        mine = _reduce_scatter(blocks, W, group).to(qh.dtype)
+        return dqh, dqt, mine[0], mine[1], mine[2], mine[3], None, None, None, None
+
+
+def lighthouse_cp_forward(xq, xk, xv, L: int, p: int, k: int, rank: int, world_size: int, group, ops=None):
+    """LighthouseCP.forward (SEL:1009-1054): (B, S_local, H, D) x3 -> (B, H, S_local, D)."""
+    ops = ops or _native
+    W = max(1, int(world_size))
+    _, s, _, _ = xq.shape
+    half = s // 2
+    k_chunk = k // (2 * W)
+    sel = []
+    for part in (slice(0, half), slice(half, s)):
+        sel.append(_SelectHalfFn.apply(xq[:, part].contiguous(), xk[:, part].contiguous(),
+                                       xv[:, part].contiguous(), L, p, k_chunk, ops))
+    (qh, kh, vh, ih, invh), (qt, kt, vt, it, invt) = sel
+    oh, ot = _CPAttentionFn.apply(qh, qt, kh, kt, vh, vt, rank, W, group, ops)
+    out_h = _ScatterInvFn.apply(oh, ih, invh, half, L, p, ops)
+    out_t = _ScatterInvFn.apply(ot, it, invt, half, L, p, ops)
+    return torch.cat([out_h, out_t], dim=2)

@@ -1,0 +1,273 @@
+// Hierarchical qk/kq chunked top-k selection, one warp per (b, h, tile).
+//
+// Semantics are those of the reference kernel
+// lighthouse_selection_chunked_topk_kernel (src/lighthouse_selection_cuda.py:114-330)
+// followed by its stable sort + gather (:425-427).  The result must be
+// bit-identical, ties included, so the comparator network is the same
+// 128-wide bitonic network (:41-110: stages k = 2..128, j = k/2..1, direction
+// desc = (i & k) == 0, swaps only on strict inequality) applied in the same
+// batch order and slot layout (:198-258).  The comparator network is an
+// algorithm that has to be alike; its execution here is different:
+//
+//  * One warp holds the 128 (score, index) pairs in registers, element i at
+//    lane i%32, register i/32.  Stages with j >= 32 are register
+//    compare-exchanges inside a thread, stages with j < 32 are xor shuffles.
+//    No shared memory, no __syncthreads inside the sort.
+//  * The qk sort carries each candidate's kq score as payload, so the kq sort
+//    of the qk rejects needs no dependent global load; the next batch's
+//    scores are prefetched while the current batch sorts.
+//  * The reference writes (ordered-float key, value) pairs and sorts them
+//    globally.  In the defined domain every candidate of every level is
+//    written exactly once and the keys order the output as a post-order walk
+//    of the refinement tree (children by position, then the refined parent,
+//    whose key c_l*(idx+1) - 2^(1-level) sorts after all its descendants).
+//    So this kernel only records which entries were refined (one bitmap per
+//    level in shared memory), sizes each coarsest entry's subtree, takes a
+//    warp prefix sum and writes the final position-ordered indices directly,
+//    plus the inverse map used by the scatter and un-pool kernels.  The
+//    per-row torch.sort / torch.gather of the reference disappear.
+#include "lh_common.cuh"
+
+namespace lh {
+
+constexpr int kSelTopk = 128;
+constexpr int kSelHalf = 64;
+constexpr float kNegBig = -1e6f;   // placeholder score (reference :191-194, :227)
+
+// One comparator stage (k, j) of the descending bitonic network.
+// NP = number of payload arrays moved with the key.
+template <int NP>
+__device__ __forceinline__ void bitonic_stage(int k, int j, int lane, float (&key)[4], float (&pf)[4],
+                                              int (&ix)[4]) {
+  if (j >= 32) {
+    const int rr = j >> 5;
+#pragma unroll
+    for (int lo = 0; lo < 4; ++lo) {
+      if (lo & rr) continue;
+      const int hi = lo | rr;
+      const int i_lo = lane + 32 * lo;
+      const bool desc = (i_lo & k) == 0;
+      const bool swap = desc ? (key[lo] < key[hi]) : (key[lo] > key[hi]);
+      if (swap) {
+        float t = key[lo]; key[lo] = key[hi]; key[hi] = t;
+        int ti = ix[lo]; ix[lo] = ix[hi]; ix[hi] = ti;
+        if (NP > 1) { float tp = pf[lo]; pf[lo] = pf[hi]; pf[hi] = tp; }
+      }
+    }
+  } else {
+    const bool lower = (lane & j) == 0;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = lane + 32 * r;
+      const bool desc = (i & k) == 0;
+      const float o = __shfl_xor_sync(0xffffffffu, key[r], j);
+      const int oi = __shfl_xor_sync(0xffffffffu, ix[r], j);
+      float op = 0.f;
+      if (NP > 1) op = __shfl_xor_sync(0xffffffffu, pf[r], j);
+      const bool swap = lower ? (desc ? (key[r] < o) : (key[r] > o)) : (desc ? (key[r] > o) : (key[r] < o));
+      if (swap) { key[r] = o; ix[r] = oi; if (NP > 1) pf[r] = op; }
+    }
+  }
+}
+
+template <int NP>
+__device__ __forceinline__ void bitonic128(int lane, float (&key)[4], float (&pf)[4], int (&ix)[4]) {
+#pragma unroll
+  for (int k = 2; k <= kSelTopk; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) bitonic_stage<NP>(k, j, lane, key, pf, ix);
+  }
+}
+
+struct SelGeom {
+  int N, L, p, shift, T, ncc, S_tot, S_sel, chunk_len;
+  int bm_word_off[8];   // bitmap word offset for reference level `lev` (2..L)
+  int bm_words;
+};
+
+// Reference level `lev` (1 = raw tokens, L = coarsest) is pyramid level lev-1.
+__device__ __forceinline__ bool refined(const uint32_t* bm, const SelGeom& g, int lev, int idx, int tile) {
+  if (lev < 2) return false;
+  const int start = tile * (g.ncc << ((g.L - lev) * g.shift));
+  const int rel = idx - start;
+  return (bm[g.bm_word_off[lev] + (rel >> 5)] >> (rel & 31)) & 1u;
+}
+
+__global__ void __launch_bounds__(32)
+select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ sk_all, SelGeom g,
+                   Pyramid pyr, int32_t* __restrict__ indices, int32_t* __restrict__ inverse) {
+  extern __shared__ uint32_t s_dyn[];
+  int* s_parent = reinterpret_cast<int*>(s_dyn);            // [128]
+  uint32_t* s_bm = s_dyn + kSelTopk;                        // refinement bitmaps
+  const int lane = threadIdx.x;
+  const int bh = blockIdx.x / g.T;
+  const int tile = blockIdx.x % g.T;
+  const float* sq = sq_all + (size_t)bh * g.S_tot;
+  const float* sk = sk_all + (size_t)bh * g.S_tot;
+  for (int w = lane; w < g.bm_words; w += 32) s_bm[w] = 0u;
+  for (int i = lane; i < kSelTopk; i += 32) s_parent[i] = -1;
+  __syncwarp();
+
+  const int pmask = g.p - 1;
+  for (int lev = g.L; lev >= 2; --lev) {
+    const int lvl_off = pyr.off[lev - 1];
+    const int K_end = pyr.len[lev - 1] - 1;
+    const int ncand = (lev == g.L) ? g.ncc : g.p * kSelTopk;
+    const int tile_start = tile * g.ncc;
+    auto cand = [&](int c) -> int {
+      if (c >= ncand) return -1;
+      if (lev == g.L) return tile_start + c;
+      const int pv = s_parent[c >> g.shift];
+      if (pv < 0) return -1;
+      const int kidx = pv * g.p + (c & pmask);
+      return (kidx > K_end) ? -1 : kidx;
+    };
+    auto valid = [&](int kidx) { return kidx >= 0 && kidx <= K_end; };
+
+    // qk arrays (regs 0,1 = running top-64 by qk; regs 2,3 = new batch)
+    float qs[4], ks[4];
+    int ix[4];
+    // kq top-64 (regs 0,1 of the kq sort)
+    float tks[2];
+    int tki[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) { qs[r] = kNegBig; ks[r] = kNegBig; ix[r] = -1; tks[r] = kNegBig; tki[r] = -1; }
+
+    const int nb = (ncand + kSelHalf - 1) / kSelHalf;
+    int nidx[2];
+    float nq[2], nk[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      nidx[r] = cand(lane + 32 * r);
+      nq[r] = valid(nidx[r]) ? __ldg(sq + lvl_off + nidx[r]) : kNegBig;
+      nk[r] = valid(nidx[r]) ? __ldg(sk + lvl_off + nidx[r]) : kNegBig;
+    }
+    for (int bt = 0; bt < nb; ++bt) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) { ix[2 + r] = nidx[r]; qs[2 + r] = nq[r]; ks[2 + r] = nk[r]; }
+      if (bt + 1 < nb) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          nidx[r] = cand((bt + 1) * kSelHalf + lane + 32 * r);
+          nq[r] = valid(nidx[r]) ? __ldg(sq + lvl_off + nidx[r]) : kNegBig;
+          nk[r] = valid(nidx[r]) ? __ldg(sk + lvl_off + nidx[r]) : kNegBig;
+        }
+      }
+      // qk sort of [top-64 by qk ; batch]          (reference :203-232)
+      bitonic128<2>(lane, qs, ks, ix);
+      // kq sort of [top-64 by kq ; qk rejects]     (reference :242-253)
+      float kk[4] = {tks[0], tks[1], ks[2], ks[3]};
+      int ki[4] = {tki[0], tki[1], ix[2], ix[3]};
+      float dummy[4];
+      bitonic128<1>(lane, kk, dummy, ki);
+      tks[0] = kk[0]; tks[1] = kk[1]; tki[0] = ki[0]; tki[1] = ki[1];
+    }
+    __syncwarp();
+    // Parents of the next level: [top-64 by qk ; top-64 by kq] (reference :324-327)
+    s_parent[lane] = ix[0];
+    s_parent[32 + lane] = ix[1];
+    s_parent[64 + lane] = tki[0];
+    s_parent[96 + lane] = tki[1];
+    const int start = tile * (g.ncc << ((g.L - lev) * g.shift));
+    const int kept[4] = {ix[0], ix[1], tki[0], tki[1]};
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int rel = kept[r] - start;
+      if (kept[r] >= 0) atomicOr(&s_bm[g.bm_word_off[lev] + (rel >> 5)], 1u << (rel & 31));
+    }
+    __syncwarp();
+  }
+
+  // ---- placement: post-order walk of each coarsest entry's refinement tree
+  const int per_lane = g.ncc / 32;
+  const int e0 = tile * g.ncc + lane * per_lane;
+  int count = 0;
+  int st_lev[8], st_idx[8], st_c[8];
+  for (int e = e0; e < e0 + per_lane; ++e) {
+    int d = 0;
+    st_lev[0] = g.L; st_idx[0] = e; st_c[0] = 0;
+    while (d >= 0) {
+      const int lev = st_lev[d], idx = st_idx[d];
+      if (st_c[d] < g.p && refined(s_bm, g, lev, idx, tile)) {
+        const int c = st_c[d]++;
+        ++d; st_lev[d] = lev - 1; st_idx[d] = idx * g.p + c; st_c[d] = 0;
+      } else {
+        ++count; --d;
+      }
+    }
+  }
+  int incl = count;
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, m);
+    if (lane >= m) incl += v;
+  }
+  int slot = tile * g.chunk_len + incl - count;
+  int32_t* out = indices + (size_t)bh * g.S_sel;
+  int32_t* inv = inverse ? inverse + (size_t)bh * g.S_tot : nullptr;
+  for (int e = e0; e < e0 + per_lane; ++e) {
+    int d = 0;
+    st_lev[0] = g.L; st_idx[0] = e; st_c[0] = 0;
+    while (d >= 0) {
+      const int lev = st_lev[d], idx = st_idx[d];
+      if (st_c[d] < g.p && refined(s_bm, g, lev, idx, tile)) {
+        const int c = st_c[d]++;
+        ++d; st_lev[d] = lev - 1; st_idx[d] = idx * g.p + c; st_c[d] = 0;
+      } else {
+        const int pidx = idx + pyr.off[lev - 1];
+        out[slot] = pidx;
+        if (inv) inv[pidx] = slot;
+        ++slot; --d;
+      }
+    }
+  }
+}
+
+// Host-side domain check; mirrors the reference asserts (CU:370-375, 385, 391)
+// and adds the conditions under which the reference kernel is well defined.
+int select_geometry(int S, int L, int p, int k, SelGeom* g, Pyramid* pyr) {
+  if (L < 2 || L > 7) { set_error("select: num_levels must be in [2, 7], got %d", L); return LH_ERR_SHAPE; }
+  if (p < 2 || (p & (p - 1))) { set_error("select: pooling_factor must be a power of 2 >= 2, got %d", p); return LH_ERR_SHAPE; }
+  if (k % 128) { set_error("select: topk must be a multiple of 128, got %d", k); return LH_ERR_SHAPE; }
+  if (k / 2 < p) { set_error("select: topk/2 must be >= pooling_factor"); return LH_ERR_SHAPE; }
+  const long long G = ipow(p, L - 1);
+  if (S % G) { set_error("select: S=%d must be a multiple of p^(L-1)=%lld", S, G); return LH_ERR_SHAPE; }
+  const int T = k / 128;
+  const long long C = S / G;
+  if (C % T) { set_error("select: coarsest length %lld not divisible by k/128=%d (reference kernel undefined)", C, T); return LH_ERR_SHAPE; }
+  const int ncc = (int)(C / T);
+  if (ncc < 128) { set_error("select: N_CHUNK_COARSEST=%d must be >= 128 (reference asserts, CU:391)", ncc); return LH_ERR_SHAPE; }
+  if (ncc % 64) { set_error("select: N_CHUNK_COARSEST=%d must be a multiple of 64 (reference kernel undefined)", ncc); return LH_ERR_SHAPE; }
+  pyr->init(S, L, p);
+  g->N = S; g->L = L; g->p = p; g->T = T; g->ncc = ncc;
+  g->shift = 0; while ((1 << g->shift) < p) ++g->shift;
+  g->S_tot = pyr->total;
+  g->S_sel = (int)sel_len(S, L, p, k);
+  g->chunk_len = (int)sel_len(S / T, L, p, 128);
+  int words = 0;
+  for (int lev = 0; lev < 8; ++lev) g->bm_word_off[lev] = 0;
+  for (int lev = 2; lev <= L; ++lev) {
+    g->bm_word_off[lev] = words;
+    words += (int)(((long long)ncc * ipow(p, L - lev) + 31) / 32);
+  }
+  g->bm_words = words;
+  return LH_OK;
+}
+
+int select_topk(const float* sqk, const float* skq, int B, int H, int S, int L, int p, int k,
+                int32_t* indices, int32_t* inverse, cudaStream_t st) {
+  SelGeom g; Pyramid pyr;
+  int rc = select_geometry(S, L, p, k, &g, &pyr);
+  if (rc) return rc;
+  const size_t smem = (kSelTopk + (size_t)g.bm_words) * sizeof(uint32_t);
+  if (smem > 200 * 1024) { set_error("select: refinement bitmaps exceed shared memory"); return LH_ERR_SHAPE; }
+  if (smem > 48 * 1024) cudaFuncSetAttribute(select_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (inverse) {
+    cudaError_t e = cudaMemsetAsync(inverse, 0xff, sizeof(int32_t) * (size_t)B * H * g.S_tot, st);
+    if (e != cudaSuccess) { set_error("select: memset inverse: %s", cudaGetErrorString(e)); return LH_ERR_LAUNCH; }
+  }
+  select_topk_kernel<<<B * H * g.T, 32, smem, st>>>(sqk, skq, g, pyr, indices, inverse);
+  return check_launch("select_topk_kernel");
+}
+
+}  // namespace lh

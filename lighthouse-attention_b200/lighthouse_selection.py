@@ -1,0 +1,220 @@
+"""Drop-in for the reference module ``lighthouse_selection`` (norm scorer path).
+
+Exports the names the torchtitan patch imports (lighthouse-attention.patch:591-598)
+with the reference's constructor arguments and forward contracts
+(src/lighthouse_selection.py of the reference, cited as SEL):
+
+  DialatedLighthouseNormScorer / DialatedLighthouseNormScorerCP   SEL:578-616, 943-982
+  LighthouseLocal                                                  SEL:772-825
+  LighthouseCP (+ set_cp_info)                                     SEL:985-1054
+  scatter_to_base_sequence                                         SEL:758-770
+  compute_output_indices_selection                                 SEL:338-354
+  DilatedLighthouseScorer, DilatedLighthouseGLAScorer              SEL:618, 692 (not provided:
+                                                                   constructing works, forward raises)
+
+``LighthouseLocal.forward`` runs the whole layer as one autograd node over
+the sm_100a kernels: pyramid + scores -> selection -> gather -> tcgen05
+causal attention -> deterministic fan-out scatter, and in backward the
+scatter adjoint -> attention backward -> un-pool.  No Triton, no fallback.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+
+from . import _native
+from .lighthouse_selection_cuda import (LighthouseSelectionQkKqChunkedTopkNvrtc,  # noqa: F401
+                                        compute_output_indices_selection)
+
+__all__ = [
+    "DialatedLighthouseNormScorer", "DialatedLighthouseNormScorerCP", "DilatedLighthouseScorer",
+    "DilatedLighthouseGLAScorer", "LighthouseLocal", "LighthouseCP", "scatter_to_base_sequence",
+    "compute_output_indices_selection", "LighthouseSelectionQkKqChunkedTopkNvrtc", "lighthouse_attention",
+]
+
+
+# ----------------------------------------------------------------------------- scorer
+class _PyramidFn(torch.autograd.Function):
+    """Scorer as an autograd node: forward = pyramid kernel; backward = un-pool
+    kernel with the identity slot map (every pyramid entry is its own slot)."""
+
+    @staticmethod
+    def forward(ctx, xq, xk, xv, L, p):
+        B, S, H, D = xq.shape
+        pq, pk, pv, sqk, skq = _native.pyramid_score(xq, xk, xv, L, p)
+        cat = lambda x, pooled: torch.cat([x.transpose(1, 2), pooled], dim=2)
+        ctx.L, ctx.p, ctx.S = L, p, S
+        ctx.mark_non_differentiable(sqk, skq)
+        return sqk.to(xq.dtype), skq.to(xq.dtype), cat(xq, pq), cat(xk, pk), cat(xv, pv)
+
+    @staticmethod
+    def backward(ctx, _gs1, _gs2, gq, gk, gv):
+        S_tot = gq.shape[2] if gq is not None else (gk if gk is not None else gv).shape[2]
+        B, H = (gq if gq is not None else (gk if gk is not None else gv)).shape[:2]
+        dev = (gq if gq is not None else (gk if gk is not None else gv)).device
+        ident = torch.arange(S_tot, dtype=torch.int32, device=dev).expand(B, H, S_tot).contiguous()
+        dq, dk, dv = _native.unpool_bwd([gq, gk, gv], ident, ctx.S, ctx.L, ctx.p)
+        return dq, dk, dv, None, None
+
+
+class DialatedLighthouseNormScorer(nn.Module):
+    """Norm scorer + pyramid (SEL:578-616).
+
+    forward(xq, xk, xv) with (B, S, H, D) inputs returns
+    (scores_qk_cat, scores_kq_cat, xq_cat, xk_cat, xv_cat): scores (B, H, S_tot)
+    in the input dtype, pyramids (B, H, S_tot, D).  The scores carry no
+    gradient (the reference only ever uses them under no_grad, SEL:794).
+    """
+
+    def __init__(self, pooling_factor: int = 4, levels: int = 3):
+        super().__init__()
+        self.pooling_factor = pooling_factor
+        self.levels = levels
+
+    def forward(self, xq, xk, xv):
+        return _PyramidFn.apply(xq, xk, xv, self.levels, self.pooling_factor)
+
+
+class DialatedLighthouseNormScorerCP(DialatedLighthouseNormScorer):
+    """CP twin of the norm scorer (SEL:943-982); identical computation."""
+
+    def __init__(self, pooling_factor: int = 4, levels: int = 3):
+        super().__init__(pooling_factor, levels)
+        self._checked = False
+
+
+class DilatedLighthouseScorer(nn.Module):
+    """Present so the torchtitan patch imports resolve (SEL:618-689). Only the
+    `norm` scorer is provided by this package."""
+
+    def __init__(self, *args, **kwargs):
+        super().__init__()
+
+    def forward(self, *args, **kwargs):
+        raise NotImplementedError("lighthouse_b200 provides the `norm` scorer only")
+
+
+class DilatedLighthouseGLAScorer(DilatedLighthouseScorer):
+    """Present so the torchtitan patch imports resolve (SEL:692-755)."""
+
+
+# ----------------------------------------------------------------------------- scatter
+class _ScatterFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, attn, indices, N_shard, N_total, L, p):
+        idx = indices.to(torch.int32).contiguous()
+        inv = _native.build_inverse(idx, _native.pyramid_len(N_shard, L, p))
+        ctx.save_for_backward(idx)
+        ctx.args = (N_shard, N_total, L, p)
+        return _native.scatter_fwd(attn, inv, N_shard, N_total, L, p)
+
+    @staticmethod
+    def backward(ctx, dout):
+        (idx,) = ctx.saved_tensors
+        return _native.scatter_bwd(dout, idx, *ctx.args), None, None, None, None, None
+
+
+def scatter_to_base_sequence(attn_out, indices_hp, rank_ids_hp, N_shard: int, N_total: int, num_levels: int,
+                             pooling_factor: int):
+    """Fan-out of selected outputs to base positions (SEL:758-770, kernels SEL:408-576).
+
+    The reference adds rank_id * N_shard to every position; its callers always
+    pass zeros (SEL:817, 1048-1049), which is the only case supported here.
+    """
+    if rank_ids_hp is not None and bool((rank_ids_hp != 0).any()):
+        raise ValueError("scatter_to_base_sequence: non-zero rank_ids are not supported")
+    return _ScatterFn.apply(attn_out, indices_hp, N_shard, N_total, num_levels, pooling_factor)
+
+
+# ----------------------------------------------------------------------------- fused layer
+class _LighthouseLayerFn(torch.autograd.Function):
+    """One Lighthouse layer (SEL:789-825) as a single autograd node."""
+
+    @staticmethod
+    def forward(ctx, xq, xk, xv, L, p, k):
+        B, S, H, D = xq.shape
+        xq, xk, xv = xq.contiguous(), xk.contiguous(), xv.contiguous()
+        pq, pk, pv, sqk, skq = _native.pyramid_score(xq, xk, xv, L, p)
+        idx, inv = _native.select_topk(sqk, skq, L, p, k, S)
+        qs, ks, vs = _native.gather_selected([xq, xk, xv], [pq, pk, pv], idx)
+        scale = 1.0 / math.sqrt(D)
+        o, lse = _native.attn_fwd(qs, ks, vs, scale)
+        out = _native.scatter_fwd(o, inv, S, S, L, p)
+        ctx.save_for_backward(qs, ks, vs, o, lse, idx, inv)
+        ctx.args = (S, L, p, scale)
+        ctx.mark_non_differentiable(idx)
+        return out, idx
+
+    @staticmethod
+    def backward(ctx, dout, _didx):
+        qs, ks, vs, o, lse, idx, inv = ctx.saved_tensors
+        S, L, p, scale = ctx.args
+        dattn = _native.scatter_bwd(dout, idx, S, S, L, p)
+        dqs, dks, dvs = _native.attn_bwd(qs, ks, vs, o, lse, dattn, scale)
+        dxq, dxk, dxv = _native.unpool_bwd([dqs, dks, dvs], inv, S, L, p)
+        return dxq, dxk, dxv, None, None, None
+
+
+def lighthouse_attention(xq, xk, xv, num_levels: int = 3, pooling_factor: int = 4, topk: int = 1024,
+                         return_indices: bool = False):
+    """Functional form of LighthouseLocal.forward: (B,S,H,D) x3 -> (B,H,S,D)."""
+    if xq.dtype != torch.bfloat16:
+        raise ValueError("lighthouse_attention computes in bf16")
+    out, idx = _LighthouseLayerFn.apply(xq, xk, xv, num_levels, pooling_factor, topk)
+    return (out, idx) if return_indices else out
+
+
+class LighthouseLocal(nn.Module):
+    """Single-device Lighthouse layer (SEL:772-825).
+
+    ``attention`` is kept for signature compatibility; the gathered causal
+    attention runs in this package's tcgen05 kernels.
+    """
+
+    def __init__(self, attention, scorer, num_levels: int = 3, pooling_factor: int = 4, topk: int = 1024):
+        super().__init__()
+        self.scorer = scorer
+        self.num_levels = num_levels
+        self.pooling_factor = pooling_factor
+        self.topk = topk
+        self.attention = attention
+
+    def forward(self, xq, xk, xv):
+        if not isinstance(self.scorer, DialatedLighthouseNormScorer):
+            raise NotImplementedError("lighthouse_b200 implements the `norm` scorer path only")
+        return lighthouse_attention(xq, xk, xv, self.num_levels, self.pooling_factor, self.topk)
+
+
+class LighthouseCP(nn.Module):
+    """Context-parallel Lighthouse layer (SEL:985-1054).
+
+    The local shard holds the head/tail load-balanced chunks r and 2W-1-r of
+    the global sequence.  Each half is pooled and selected on its own with
+    topk / (2W) (SEL:1009-1029); attention runs causally over the selections
+    of all 2W chunks in global order, K/V of the other ranks arriving through
+    one NCCL all-gather (see ``cp.py``); each half is scattered back into its
+    own half (SEL:1046-1054).
+    """
+
+    def __init__(self, attention, scorer, num_levels: int = 3, pooling_factor: int = 4, topk: int = 1024):
+        super().__init__()
+        self.scorer = scorer
+        self.num_levels = num_levels
+        self.pooling_factor = pooling_factor
+        self.topk = topk
+        self.attention = attention
+        self._rank = 0
+        self._world_size = 1
+        self._cp_group = None
+
+    def set_cp_info(self, rank: int, world_size: int, cp_group):
+        self._rank = rank
+        self._world_size = world_size
+        self._cp_group = cp_group
+
+    def forward(self, xq, xk, xv):
+        from . import cp
+        return cp.lighthouse_cp_forward(xq, xk, xv, self.num_levels, self.pooling_factor, self.topk,
+                                        self._rank, self._world_size, self._cp_group)

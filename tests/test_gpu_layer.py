@@ -1,0 +1,69 @@
+"""End-to-end Lighthouse layer (the drop-in module API) on the GPU vs the oracle."""
+import pytest
+import torch
+
+from inputs import make_qkv
+
+pytestmark = pytest.mark.gpu
+
+
+def _err(a, b):
+    a, b = a.float(), b.float()
+    return (a - b).abs().max().item(), ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+
+
+@pytest.mark.parametrize("shape", [(1, 4096, 2, 3, 4, 256), (1, 8192, 2, 3, 2, 256), (1, 16384, 2, 4, 2, 256),
+                                   (2, 8192, 2, 2, 8, 128)])
+def test_lighthouse_local_fwd_bwd_vs_oracle(lh, O, cuda, shape):
+    B, S, H, L, p, k = shape
+    D = 128
+    xq, xk, xv = make_qkv(B, S, H, D, torch.bfloat16, 17)
+    g = torch.Generator().manual_seed(18)
+    dout = torch.randn(B, H, S, D, generator=g).to(torch.bfloat16)
+    layer = lh.LighthouseLocal(None, lh.DialatedLighthouseNormScorer(p, L), num_levels=L, pooling_factor=p, topk=k)
+    xs = [t.to(cuda).requires_grad_(True) for t in (xq, xk, xv)]
+    out = layer(*xs)
+    out.backward(dout.to(cuda))
+    # oracle on the same selection (selection parity is tested on its own)
+    _, _, _, sqk, skq = lh._native.pyramid_score(*[t.detach() for t in xs], L, p)
+    idx = O.select(sqk.cpu(), skq.cpu(), L, p, k, S)
+    xr = [t.float().requires_grad_(True) for t in (xq, xk, xv)]
+    ref, _ = O.lighthouse_local(*xr, L, p, k, indices=idx)
+    ref.backward(dout.float())
+    m, r = _err(out.cpu(), ref)
+    assert m <= 2e-2 and r <= 1e-2, f"out max-abs {m:.3e} rel {r:.3e}"
+    for a, b, n in zip(xs, xr, "qkv"):
+        m, r = _err(a.grad.cpu(), b.grad)
+        assert m <= 2e-2 and r <= 1e-2, f"d{n} max-abs {m:.3e} rel {r:.3e}"
+    assert lh._native.device_status() == 0
+
+
+def test_lighthouse_cp_single_rank_vs_oracle(lh, O, cuda):
+    B, S, H, D, L, p, k = 1, 16384, 2, 128, 3, 4, 1024
+    xq, xk, xv = make_qkv(B, S, H, D, torch.bfloat16, 19)
+    layer = lh.LighthouseCP(None, lh.DialatedLighthouseNormScorerCP(p, L), num_levels=L, pooling_factor=p, topk=k)
+    xs = [t.to(cuda).requires_grad_(True) for t in (xq, xk, xv)]
+    out = layer(*xs)
+    dout = torch.randn_like(out)
+    out.backward(dout)
+    xr = [t.float().requires_grad_(True) for t in (xq, xk, xv)]
+    ref, _ = O.lighthouse_cp_global(*xr, 1, L, p, k)
+    ref.backward(dout.float().cpu())
+    m, r = _err(out.cpu(), ref)
+    # selections may differ where a bf16 norm rounds differently; compare loosely
+    assert r <= 2e-2, f"cp out rel {r:.3e}"
+
+
+def test_scorer_module_api(lh, O, cuda):
+    B, S, H, D, L, p = 1, 4096, 2, 128, 3, 4
+    xq, xk, xv = (t.to(cuda).requires_grad_(True) for t in make_qkv(B, S, H, D, torch.bfloat16, 20))
+    sqk, skq, qc, kc, vc = lh.DialatedLighthouseNormScorer(p, L)(xq, xk, xv)
+    rq, rk, rqc, rkc, rvc = O.norm_scorer(xq.detach(), xk.detach(), xv.detach(), p, L)
+    assert sqk.dtype == torch.bfloat16 and sqk.shape == rq.shape and qc.shape == rqc.shape
+    assert (sqk.float() - rq.float()).abs().max().item() <= 0.1
+    (qc.float().sum() + 2 * kc.float().sum() + 3 * vc.float().sum()).backward()
+    xr = [t.detach().float().requires_grad_(True) for t in (xq, xk, xv)]
+    _, _, a, b, c = O.norm_scorer(*xr, p, L)
+    (a.sum() + 2 * b.sum() + 3 * c.sum()).backward()
+    for x, y in zip((xq, xk, xv), xr):
+        assert (x.grad.float() - y.grad).abs().max().item() < 1e-2

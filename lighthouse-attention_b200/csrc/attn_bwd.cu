@@ -1,12 +1,392 @@
-// Causal attention backward (placeholder until the tcgen05 kernel lands).
+// Causal attention backward on tcgen05 / TMEM (dQ, dK, dV).
+//
+// Backward of F.scaled_dot_product_attention(is_causal=True) on the selected
+// sequence (reference src/lighthouse_selection.py:815), with the same causal
+// geometry as attn_fwd.cu (query row r at position q_off + r, key row c at c).
+//
+// Three launches:
+//   1. prep:  Delta[q] = sum_d dO[q,d] * O[q,d] (fp32), dQacc = 0
+//   2. main:  one CTA per (128-key tile j, b*h); K_j and V_j stay in shared
+//             memory while the CTA walks every query tile i that can see them:
+//               S^T  = K_j Q_i^T             (SS, TMEM cols   0..127)
+//               dP^T = V_j dO_i^T            (SS, TMEM cols 128..255)
+//             softmax warps (one key row per thread = TMEM lane):
+//               P^T  = exp2(S^T * scale*log2e - lse2[q])  -> bf16 into TMEM cols 0..63
+//               dS^T = P^T * (dP^T - Delta[q])            -> bf16 into shared memory
+//               dV_j += P^T dO_i             (TS, TMEM cols 256..383)
+//               dK_j += dS^T Q_i             (SS, TMEM cols 384..511)
+//               dQ_i  = dS K_j               (SS, dS read MN-major; TMEM cols 128..255)
+//             the softmax warps then drain dQ_i from TMEM into the fp32 dQacc
+//             with vector atomics.  At the end dK (times scale) and dV are
+//             written as bf16.
+//   3. post:  dQ = bf16(dQacc * scale)
+// Shared-memory operands use the 128-byte swizzle; Q_i / dO_i / K_j / V_j
+// arrive by TMA (no multicast).  Every mbarrier wait is bounded.
+#include <cudaTypedefs.h>
+
 #include "lh_common.cuh"
+#include "sm100.cuh"
+
 namespace lh {
+
+using namespace sm100;
+
+__device__ int g_attn_bwd_status;   // set to 1 when a bounded wait gave up
+int make_tmap_rows(CUtensorMap* m, const void* ptr, int rows, int BH);
+
+namespace bwd {
+constexpr int kTile = 128;
+constexpr int kD = 128;
+constexpr int kBox = 16384;
+constexpr int kTileBytes = 2 * kBox;
+constexpr int kThreads = 192;
+constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384, kTmemCols = 512;
+}  // namespace bwd
+
+struct BwdSmem {
+  uint64_t kv_full, q_full, q_empty, s_ready, p_ready, dq_ready, dq_free;
+  uint32_t tmem_base;
+  int abort;
+  float lse2[2][bwd::kTile];
+  float delta[2][bwd::kTile];
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 16-byte store of 8 bf16 into the SW128 K-major layout of a 128 x 128 tile
+// stored as two 64-column boxes: row r, columns [8c, 8c+8).
+__device__ __forceinline__ void st_sw128(uint8_t* tile, int r, int c, uint4 v) {
+  const int box = c >> 3, chunk = c & 7;
+  *reinterpret_cast<uint4*>(tile + box * bwd::kBox + r * 128 + ((chunk ^ (r & 7)) << 4)) = v;
+}
+
+__global__ void __launch_bounds__(bwd::kThreads, 1)
+attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                const float* __restrict__ LSE, const float* __restrict__ Delta, float* __restrict__ dQacc,
+                __nv_bfloat16* __restrict__ dK, __nv_bfloat16* __restrict__ dV, int S_q, int S_kv, int q_off,
+                float scale2, float scale) {
+  using namespace bwd;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = base;
+  uint8_t* sV = base + kTileBytes;
+  uint8_t* sQ = base + 2 * kTileBytes;
+  uint8_t* sdO = base + 3 * kTileBytes;
+  uint8_t* sdS = base + 4 * kTileBytes;
+  BwdSmem* sm = reinterpret_cast<BwdSmem*>(base + 5 * kTileBytes);
+
+  const int bh = blockIdx.x;
+  const int j = blockIdx.y;                      // key tile (heaviest first: j = 0 sees every query)
+  const int n_qt = (S_q + kTile - 1) / kTile;
+  int i0 = (j * kTile - q_off) / kTile;          // first query tile with a row at position >= j*128
+  if (j * kTile - q_off < 0) i0 = 0;
+  const int n_it = n_qt - i0 > 0 ? n_qt - i0 : 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (*reinterpret_cast<volatile int*>(&g_attn_bwd_status)) return;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm->kv_full, 1);
+    mbar_init(&sm->q_full, 1);
+    mbar_init(&sm->q_empty, 1);
+    mbar_init(&sm->s_ready, 1);
+    mbar_init(&sm->p_ready, 128);
+    mbar_init(&sm->dq_ready, 1);
+    mbar_init(&sm->dq_free, 128);
+    sm->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&sm->tmem_base, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm->tmem_base;
+  volatile int* abort = &sm->abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && n_it > 0) {
+      mbar_expect_tx(&sm->kv_full, 2 * kTileBytes);
+      tma_load_3d(sK, &tmK, &sm->kv_full, 0, j * kTile, bh);
+      tma_load_3d(sK + kBox, &tmK, &sm->kv_full, 64, j * kTile, bh);
+      tma_load_3d(sV, &tmV, &sm->kv_full, 0, j * kTile, bh);
+      tma_load_3d(sV + kBox, &tmV, &sm->kv_full, 64, j * kTile, bh);
+    }
+    for (int t = 0; t < n_it; ++t) {
+      if (t > 0) {
+        bool ok = mbar_wait(&sm->q_empty, (t - 1) & 1, abort);
+        if (__any_sync(0xffffffffu, !ok)) break;
+      }
+      if (lane == 0) {
+        const int i = i0 + t;
+        mbar_expect_tx(&sm->q_full, 2 * kTileBytes);
+        tma_load_3d(sQ, &tmQ, &sm->q_full, 0, i * kTile, bh);
+        tma_load_3d(sQ + kBox, &tmQ, &sm->q_full, 64, i * kTile, bh);
+        tma_load_3d(sdO, &tmdO, &sm->q_full, 0, i * kTile, bh);
+        tma_load_3d(sdO + kBox, &tmdO, &sm->q_full, 64, i * kTile, bh);
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t id_kk = idesc_bf16_f32(kTile, kTile, false, false);   // A K-major, B K-major
+    constexpr uint32_t id_kmn = idesc_bf16_f32(kTile, kD, false, true);      // A K-major, B MN-major
+    constexpr uint32_t id_mnmn = idesc_bf16_f32(kTile, kD, true, true);      // A MN-major, B MN-major
+    const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO),
+                   adS = smem_u32(sdS);
+    bool ok = n_it > 0 ? mbar_wait(&sm->kv_full, 0, abort) : true;
+    for (int t = 0; t < n_it; ++t) {
+      ok = ok && mbar_wait(&sm->q_full, t & 1, abort);
+      if (t > 0) ok = ok && mbar_wait(&sm->dq_free, (t - 1) & 1, abort);
+      if (__any_sync(0xffffffffu, !ok)) break;
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+          mma_ss(tbase + kColS, smem_desc_sw128(aK + off, 16, 1024), smem_desc_sw128(aQ + off, 16, 1024), id_kk,
+                 kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+          mma_ss(tbase + kColDP, smem_desc_sw128(aV + off, 16, 1024), smem_desc_sw128(adO + off, 16, 1024), id_kk,
+                 kk > 0);
+        }
+        mma_commit(&sm->s_ready);
+      }
+      __syncwarp();
+      ok = mbar_wait(&sm->p_ready, t & 1, abort);
+      if (__any_sync(0xffffffffu, !ok)) break;
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)   // dV += P^T dO   (K = query rows)
+          mma_ts(tbase + kColDV, tbase + kColS + kk * 8, smem_desc_sw128(adO + kk * 2048, kBox, 1024), id_kmn,
+                 (t > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {  // dK += dS^T Q
+          const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+          mma_ss(tbase + kColDK, smem_desc_sw128(adS + off, 16, 1024), smem_desc_sw128(aQ + kk * 2048, kBox, 1024),
+                 id_kmn, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)    // dQ_i = dS K   (K = key rows)
+          mma_ss(tbase + kColDP, smem_desc_sw128(adS + kk * 2048, kBox, 1024),
+                 smem_desc_sw128(aK + kk * 2048, kBox, 1024), id_mnmn, kk > 0);
+        mma_commit(&sm->dq_ready);
+        mma_commit(&sm->q_empty);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ softmax / dS / drain
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;                 // key row inside the tile (TMEM lane)
+    const int tid = threadIdx.x - 64;               // 0..127
+    const int kv_pos = j * kTile + r;
+    const uint32_t lane_base = tbase + ((uint32_t)(quad * 32) << 16);
+    bool ok = true;
+    for (int t = 0; t < n_it && ok; ++t) {
+      const int i = i0 + t;
+      const int buf = t & 1;
+      {
+        const int q = i * kTile + tid;
+        sm->lse2[buf][tid] = q < S_q ? LSE[(size_t)bh * S_q + q] * 1.4426950408889634f : INFINITY;
+        sm->delta[buf][tid] = q < S_q ? Delta[(size_t)bh * S_q + q] : 0.f;
+      }
+      named_bar_sync(1, 128);
+      ok = mbar_wait(&sm->s_ready, t & 1, abort);
+      if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+      tc_fence_after();
+      const int q_lo = q_off + i * kTile;
+      const bool need_mask = (j * kTile + kTile - 1 > q_lo) || (i * kTile + kTile > S_q) || (j * kTile + kTile > S_kv);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {               // 64 query columns per half
+        uint32_t pk[32];
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          const int c = h * 2 + c2;                 // 32-column chunk
+          uint32_t s[32], dp[32];
+          tmem_ld32(lane_base + kColS + c * 32, s);
+          tmem_ld32(lane_base + kColDP + c * 32, dp);
+          tmem_ld_wait();
+          uint32_t dsw[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float pr[2], dr[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int ql = c * 32 + e + u;
+              float p = ex2(fmaf(__uint_as_float(s[e + u]), scale2, -sm->lse2[buf][ql]));
+              if (need_mask) {
+                const int qpos = q_lo + ql;
+                if (kv_pos > qpos || i * kTile + ql >= S_q || kv_pos >= S_kv) p = 0.f;
+              }
+              pr[u] = p;
+              dr[u] = p * (__uint_as_float(dp[e + u]) - sm->delta[buf][ql]);
+            }
+            pk[c2 * 16 + e / 2] = pack_bf16(pr[0], pr[1]);
+            dsw[e / 2] = pack_bf16(dr[0], dr[1]);
+          }
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            st_sw128(sdS, r, c * 4 + v, make_uint4(dsw[4 * v], dsw[4 * v + 1], dsw[4 * v + 2], dsw[4 * v + 3]));
+        }
+        tmem_st32(lane_base + kColS + h * 32, pk);
+      }
+      tmem_st_wait();
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&sm->p_ready);
+      // drain dQ_i: TMEM lane = query row
+      ok = mbar_wait(&sm->dq_ready, t & 1, abort);
+      if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+      tc_fence_after();
+      const int qrow = i * kTile + r;
+      float* dst = dQacc + ((size_t)bh * S_q + qrow) * kD;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(lane_base + kColDP + c * 32, v);
+        tmem_ld_wait();
+        if (qrow < S_q) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + e),
+                      make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]), __uint_as_float(v[e + 2]),
+                                  __uint_as_float(v[e + 3])));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sm->dq_free);
+    }
+    // epilogue: dV and dK rows of this key tile
+    if (!__any_sync(0xffffffffu, !ok)) {
+      tc_fence_after();
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t col = which == 0 ? kColDV : kColDK;
+        const float mul = which == 0 ? 1.0f : scale;
+        __nv_bfloat16* row = (which == 0 ? dV : dK) + ((size_t)bh * S_kv + kv_pos) * kD;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          if (n_it > 0) {
+            tmem_ld32(lane_base + col + c * 32, v);
+            tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = 0u;
+          }
+          if (kv_pos < S_kv) {
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4) {
+              uint4 w;
+              w.x = pack_bf16(__uint_as_float(v[v4 * 8 + 0]) * mul, __uint_as_float(v[v4 * 8 + 1]) * mul);
+              w.y = pack_bf16(__uint_as_float(v[v4 * 8 + 2]) * mul, __uint_as_float(v[v4 * 8 + 3]) * mul);
+              w.z = pack_bf16(__uint_as_float(v[v4 * 8 + 4]) * mul, __uint_as_float(v[v4 * 8 + 5]) * mul);
+              w.w = pack_bf16(__uint_as_float(v[v4 * 8 + 6]) * mul, __uint_as_float(v[v4 * 8 + 7]) * mul);
+              *reinterpret_cast<uint4*>(row + c * 32 + v4 * 8) = w;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+  if (threadIdx.x == 0 && sm->abort) atomicExch(&g_attn_bwd_status, 1);
+}
+
+// Delta = rowsum(dO * O) in fp32; zero dQacc.  One warp per query row.
+__global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ O, const __nv_bfloat16* __restrict__ dO,
+                                     float* __restrict__ Delta, float* __restrict__ dQacc, long long rows) {
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= rows) return;
+  const size_t off = (size_t)w * 128 + lane * 4;
+  const uint2 a = *reinterpret_cast<const uint2*>(O + off);
+  const uint2 b = *reinterpret_cast<const uint2*>(dO + off);
+  const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
+  float2 a0 = __bfloat1622float2(ha[0]), a1 = __bfloat1622float2(ha[1]);
+  float2 b0 = __bfloat1622float2(hb[0]), b1 = __bfloat1622float2(hb[1]);
+  float s = a0.x * b0.x + a0.y * b0.y + a1.x * b1.x + a1.y * b1.y;
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+  if (lane == 0) Delta[w] = s;
+  *reinterpret_cast<float4*>(dQacc + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+__global__ void attn_bwd_post_kernel(const float* __restrict__ dQacc, __nv_bfloat16* __restrict__ dQ, float scale,
+                                     long long n8) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(dQacc)[2 * i];
+    const float4 b = reinterpret_cast<const float4*>(dQacc)[2 * i + 1];
+    uint4 w;
+    w.x = pack_bf16(a.x * scale, a.y * scale);
+    w.y = pack_bf16(a.z * scale, a.w * scale);
+    w.z = pack_bf16(b.x * scale, b.y * scale);
+    w.w = pack_bf16(b.z * scale, b.w * scale);
+    reinterpret_cast<uint4*>(dQ)[i] = w;
+  }
+}
+
+int attn_bwd_status(int reset) {
+  int h = 0;
+  cudaMemcpyFromSymbol(&h, g_attn_bwd_status, sizeof(int));
+  if (reset) { int z = 0; cudaMemcpyToSymbol(g_attn_bwd_status, &z, sizeof(int)); }
+  return h;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
 size_t attn_bwd_workspace_size(int B, int H, int S_q, int S_kv, int D) {
-  return (size_t)B * H * ((S_q + 127) / 128 * 128) * (D + 1) * sizeof(float) + 256;
+  (void)S_kv;
+  const size_t rows = (size_t)B * H * S_q;
+  return align256(rows * D * sizeof(float)) + align256(rows * sizeof(float));
 }
-int attn_bwd(const void*, const void*, const void*, const void*, const float*, const void*, int, int, int, int,
-             int, int, float, void*, void*, void*, void*, size_t, cudaStream_t) {
-  set_error("attn_bwd: not built");
-  return LH_ERR_LAUNCH;
+
+int attn_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse, const void* dO, int B,
+             int H, int S_q, int S_kv, int q_off, int D, float scale, void* dq, void* dk, void* dv, void* ws,
+             size_t ws_bytes, cudaStream_t st) {
+  (void)ws_bytes;
+  const size_t rows = (size_t)B * H * S_q;
+  float* dQacc = reinterpret_cast<float*>(ws);
+  float* Delta = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + align256(rows * D * sizeof(float)));
+  CUtensorMap mq, mk, mv, mdo;
+  int rc;
+  if ((rc = make_tmap_rows(&mq, q, S_q, B * H))) return rc;
+  if ((rc = make_tmap_rows(&mk, k, S_kv, B * H))) return rc;
+  if ((rc = make_tmap_rows(&mv, v, S_kv, B * H))) return rc;
+  if ((rc = make_tmap_rows(&mdo, dO, S_q, B * H))) return rc;
+  {
+    const long long threads = (long long)rows * 32;
+    attn_bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+        (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, Delta, dQacc, (long long)rows);
+    if ((rc = check_launch("attn_bwd_prep_kernel"))) return rc;
+  }
+  const size_t smem = 1024 + 5 * bwd::kTileBytes + sizeof(BwdSmem);
+  cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(B * H, (S_kv + bwd::kTile - 1) / bwd::kTile);
+  attn_bwd_kernel<<<grid, bwd::kThreads, smem, st>>>(mq, mk, mv, mdo, lse, Delta, dQacc, (__nv_bfloat16*)dk,
+                                                    (__nv_bfloat16*)dv, S_q, S_kv, q_off,
+                                                    scale * 1.4426950408889634f, scale);
+  if ((rc = check_launch("attn_bwd_kernel"))) return rc;
+  const long long n8 = (long long)rows * D / 8;
+  attn_bwd_post_kernel<<<148 * 8, 256, 0, st>>>(dQacc, (__nv_bfloat16*)dq, scale, n8);
+  return check_launch("attn_bwd_post_kernel");
 }
+
 }  // namespace lh

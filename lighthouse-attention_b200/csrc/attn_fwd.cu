@@ -320,9 +320,13 @@ int attn_fwd(const void* q, const void* k, const void* v, int B, int H, int S_q,
   return check_launch("attn_fwd_kernel");
 }
 
+int attn_bwd_status(int reset);
+
 int attn_status(int reset) {
-  int h = 0;
-  cudaMemcpyFromSymbol(&h, g_attn_status, sizeof(int));
+  int h = attn_bwd_status(reset);
+  int f = 0;
+  cudaMemcpyFromSymbol(&f, g_attn_status, sizeof(int));
+  h |= f;
   if (reset) { int z = 0; cudaMemcpyToSymbol(g_attn_status, &z, sizeof(int)); }
   return h;
 }

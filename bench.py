@@ -1,0 +1,302 @@
+"""Benchmark: Lighthouse attention layer forward+backward tokens/s (BASELINE metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE.json config 3 at k=2048, the metric's "@S=128K k=2048"):
+B=1, S=131072, H=8, D=128, norm scorer, L=3, p=4, k=2048, causal, bf16,
+q/k/v/dO seeded N(0,1).  One step = forward + backward of one layer.  Inputs
+(3 x 268 MB + dO) are larger than the 126 MB L2, so no flush is needed
+between steps.
+
+N > 1 (torchrun): every rank runs an independent replica (the layer has no
+parameters and the path does not shard across ranks: "replicas only"), value =
+all ranks' tokens / the max over ranks of the device time.
+
+``--impl reference`` times the reference's CPU implementation of the path
+(the oracle's restatement: ATen scorer, C selection, torch.gather, CPU SDPA,
+index_add scatter -- the reference itself has no CPU selection or scatter)
+on the host cores, on rank 0 only, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(B=1, S=131072, H=8, D=128, L=3, p=4, k=2048)
+METRIC = "Lighthouse attn fwd+bwd tokens/s @S=128K k=2048"
+
+
+def _sel_len(S, L, p, k):
+    return S // p ** (L - 1) + (L - 1) * p * k
+
+
+def _config(extra=None):
+    c = {"workload": "lighthouse_layer_fwd_bwd", "batch": CFG["B"], "seq_len": CFG["S"], "heads": CFG["H"],
+         "head_dim": CFG["D"], "levels": CFG["L"], "pooling_factor": CFG["p"], "topk": CFG["k"],
+         "selected_len": _sel_len(CFG["S"], CFG["L"], CFG["p"], CFG["k"]), "scorer": "norm",
+         "l2": "inputs larger than L2 (no flush needed)"}
+    c.update(extra or {})
+    return c
+
+
+def _inputs(device, dtype=torch.bfloat16, heads=None):
+    B, S, H, D = CFG["B"], CFG["S"], CFG["H"], CFG["D"]
+    g = torch.Generator().manual_seed(0)
+    xs = [torch.randn(B, S, H, D, generator=g) for _ in range(3)]
+    dout = torch.randn(B, H, S, D, generator=g)
+    if heads is not None:
+        xs = [x[:, :, heads].contiguous() for x in xs]
+        dout = dout[:, heads].contiguous()
+    return [x.to(dtype).to(device) for x in xs], dout.to(dtype).to(device)
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, index: int):
+        self.proc = None
+        self.index = index
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.rows = []
+        if self.proc is None:
+            return
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=5)
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 7:
+                self.rows.append(parts)
+
+    def summary(self):
+        if not getattr(self, "rows", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[3:7]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(self.rows[0][1]) if self.rows[0][1].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local_rank):
+    import __graft_entry__ as ge
+    lh = ge.load_package()
+    N = lh._native
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, S, H, D, L, p, k = (CFG[x] for x in ("B", "S", "H", "D", "L", "p", "k"))
+    (xq, xk, xv), dout = _inputs(dev)
+    scale = 1.0 / math.sqrt(D)
+    ev = {}
+
+    def mark(name):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        ev.setdefault(name, []).append(e)
+
+    def step(timed):
+        # the fused layer of lighthouse_selection._LighthouseLayerFn, instrumented
+        pq, pk, pv, sqk, skq = N.pyramid_score(xq, xk, xv, L, p)
+        idx, inv = N.select_topk(sqk, skq, L, p, k, S)
+        qs, ks, vs = N.gather_selected([xq, xk, xv], [pq, pk, pv], idx)
+        if timed: mark("fwd0")
+        o, lse = N.attn_fwd(qs, ks, vs, scale)
+        if timed: mark("fwd1")
+        out = N.scatter_fwd(o, inv, S, S, L, p)
+        dattn = N.scatter_bwd(dout, idx, S, S, L, p)
+        if timed: mark("bwd0")
+        dqs, dks, dvs = N.attn_bwd(qs, ks, vs, o, lse, dattn, scale)
+        if timed: mark("bwd1")
+        dx = N.unpool_bwd([dqs, dks, dvs], inv, S, L, p)
+        return out, dx
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step(True)
+        t1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ev["fwd0"], ev["fwd1"]))
+    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ev["bwd0"], ev["bwd1"]))
+    assert N.device_status() == 0, "an attention kernel left a bounded wait"
+
+    # end to end through the public API: pinned host inputs -> device, scalar loss back
+    (hq, hk, hv), _ = _inputs("cpu")
+    hq, hk, hv = (t.pin_memory() for t in (hq, hk, hv))
+    w = dout  # resident upstream weight: loss = <out, w>
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+
+    def e2e_step():
+        xs = [t.to(dev, non_blocking=True).requires_grad_(True) for t in (hq, hk, hv)]
+        out = lh.lighthouse_attention(*xs, num_levels=L, pooling_factor=p, topk=k)
+        loss = (out.float() * w.float()).sum()
+        loss.backward()
+        return loss.item()
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(1, min(args.steps, 5))
+    e0.record()
+    for _ in range(e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, fwd_ms, bwd_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms, fwd_ms, bwd_ms = t.tolist()
+    if rank != 0:
+        return
+
+    P = _sel_len(S, L, p, k) * (_sel_len(S, L, p, k) + 1) / 2
+    bwd_flops = 10 * B * H * D * P
+    fwd_flops = 4 * B * H * D * P
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    peak = peaks.get("bf16_tflops_sustained") or 1400.0
+    peak_src = "measured sustained" if "bf16_tflops_sustained" in peaks else "fallback"
+    achieved = bwd_flops / (bwd_ms * 1e-3) / 1e12
+    tokens = B * S * world
+    line = {
+        "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q/k/v/dO)",
+        "config": _config({"parallelism": f"replicas x{world}"}),
+        "roofline": {"kernel": "attn_bwd (prep + tcgen05 main + post)", "bound": "tensor",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": peak_src, "traffic": None,
+                     "flops_per_launch": bwd_flops, "ms_per_launch": bwd_ms},
+        "kernels": {"attn_fwd_ms": fwd_ms, "attn_fwd_tflops": fwd_flops / (fwd_ms * 1e-3) / 1e12,
+                    "attn_bwd_ms": bwd_ms, "attn_bwd_tflops": achieved,
+                    "rest_ms": ms - fwd_ms - bwd_ms},
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms, "api": "lighthouse_attention"},
+        "gpu_launches": 10 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_sample(steps=1, warmup=0)["cpu_baseline"]
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- CPU arm
+def cpu_sample(steps: int, warmup: int):
+    """The reference path on the host cores, one head of the workload per step."""
+    from oracle import oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, S, H, D, L, p, k = (CFG[x] for x in ("B", "S", "H", "D", "L", "p", "k"))
+    (xq, xk, xv), dout = _inputs("cpu", torch.float32, heads=[0])
+
+    def one():
+        xs = [t.clone().requires_grad_(True) for t in (xq, xk, xv)]
+        out, _ = O.lighthouse_local(*xs, L, p, k)
+        out.backward(dout)
+
+    for _ in range(warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    dt = (time.perf_counter() - t0) / steps
+    value = (B * S / H) / dt          # one of H heads per step
+    return {"value": value, "sec_per_step": dt, "cpu_baseline": {
+        "value": value, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+        "dtype": "f32",
+        "sample": f"1 of {H} heads of the S={S} layer fwd+bwd per step, tokens/s scaled by 1/{H}; "
+                  "oracle restatement (ATen scorer, C selection, gather, CPU SDPA, index_add scatter)"}}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 3))
+    warm = min(args.warmup, 1)
+    r = cpu_sample(steps, warm)
+    line = {"metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
+            "warmup": warm, "ms_per_step": r["sec_per_step"] * 1e3 * CFG["H"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+            "config": _config({"parallelism": "cpu"}), "impl": "reference",
+            "cpu_baseline": r["cpu_baseline"],
+            "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seq-len", type=int, default=None, help="profiling only: override S")
+    ap.add_argument("--topk", type=int, default=None, help="profiling only: override k")
+    args = ap.parse_args()
+    if args.seq_len:
+        CFG["S"] = args.seq_len
+    if args.topk:
+        CFG["k"] = args.topk
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl")
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

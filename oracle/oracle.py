@@ -253,11 +253,12 @@ def lighthouse_local(xq, xk, xv, L: int, p: int, k: int, indices=None, select_fn
     return scatter_to_base(attn, indices, s, s, L, p), indices
 
 
-def lighthouse_cp_global(xq, xk, xv, world_size: int, L: int, p: int, k: int):
+def lighthouse_cp_global(xq, xk, xv, world_size: int, L: int, p: int, k: int, indices=None):
     """Semantics of LighthouseCP (SEL:1009-1054) under load-balanced CP with
     world size W, emulated in one process on the global sequence: 2W equal
     chunks, per-chunk scorer + selection with k/(2W), one causal attention over
-    the selections concatenated in global chunk order, per-chunk scatter."""
+    the selections concatenated in global chunk order, per-chunk scatter.
+    ``indices`` (one tensor per chunk) may be given to skip selection."""
     B, S, H, D = xq.shape
     nch = 2 * world_size
     n = S // nch
@@ -267,8 +268,11 @@ def lighthouse_cp_global(xq, xk, xv, world_size: int, L: int, p: int, k: int):
     for c in range(nch):
         sl = slice(c * n, (c + 1) * n)
         sqk, skq, qc, kc_, vc = norm_scorer(xq[:, sl], xk[:, sl], xv[:, sl], p, L)
-        with torch.no_grad():
-            idx = select(sqk.float(), skq.float(), L, p, kc, n)
+        if indices is not None:
+            idx = indices[c]
+        else:
+            with torch.no_grad():
+                idx = select(sqk.float(), skq.float(), L, p, kc, n)
         idxs.append(idx)
         qs.append(gather_rows(qc, idx)); ks.append(gather_rows(kc_, idx)); vs.append(gather_rows(vc, idx))
     attn = sdpa_causal(torch.cat(qs, 2), torch.cat(ks, 2), torch.cat(vs, 2))

@@ -8,8 +8,14 @@ pytestmark = pytest.mark.gpu
 
 
 def _err(a, b):
+    """(max-abs error beyond one bf16 ulp of the reference value, rel-L2 error).
+
+    The layer's outputs and gradients are stored in bf16, so a result that is
+    exact up to its own storage rounding differs from an fp32 reference by up
+    to one bf16 ulp (2^-7 |x|); the max-abs bar of 2e-2 applies on top of it."""
     a, b = a.float(), b.float()
-    return (a - b).abs().max().item(), ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+    beyond = ((a - b).abs() - b.abs() * 2.0 ** -7).clamp_min(0).max().item()
+    return beyond, ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
 
 
 @pytest.mark.parametrize("shape", [(1, 4096, 2, 3, 4, 256), (1, 8192, 2, 3, 2, 256), (1, 16384, 2, 4, 2, 256),
@@ -46,12 +52,20 @@ def test_lighthouse_cp_single_rank_vs_oracle(lh, O, cuda):
     out = layer(*xs)
     dout = torch.randn_like(out)
     out.backward(dout)
+    # per-chunk selections from the kernels (selection parity is tested on its own)
+    half = S // 2
+    idxs = []
+    for part in (slice(0, half), slice(half, S)):
+        _, _, _, sqk, skq = lh._native.pyramid_score(*[t.detach()[:, part].contiguous() for t in xs], L, p)
+        idxs.append(O.select(sqk.cpu(), skq.cpu(), L, p, k // 2, half))
     xr = [t.float().requires_grad_(True) for t in (xq, xk, xv)]
-    ref, _ = O.lighthouse_cp_global(*xr, 1, L, p, k)
+    ref, _ = O.lighthouse_cp_global(*xr, 1, L, p, k, indices=idxs)
     ref.backward(dout.float().cpu())
     m, r = _err(out.cpu(), ref)
-    # selections may differ where a bf16 norm rounds differently; compare loosely
-    assert r <= 2e-2, f"cp out rel {r:.3e}"
+    assert m <= 2e-2 and r <= 1e-2, f"cp out max-abs {m:.3e} rel {r:.3e}"
+    for a, b, n in zip(xs, xr, "qkv"):
+        m, r = _err(a.grad.cpu(), b.grad)
+        assert m <= 2e-2 and r <= 1e-2, f"cp d{n} max-abs {m:.3e} rel {r:.3e}"
 
 
 def test_scorer_module_api(lh, O, cuda):

@@ -122,6 +122,21 @@ int lh_attn_bwd(const void* q, const void* k, const void* v, const void* o, cons
                 void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
                 void* stream);
 
+/* Allocation-free lh_attn_bwd, for callers that may not allocate device memory
+ * during a step (a foreign-language host without PyTorch's caching allocator,
+ * where cudaMalloc would also synchronise mid-step, or a process whose device
+ * memory pool is fixed up front).  It has no counterpart in the reference.
+ * Same arguments and results as lh_attn_bwd without the workspace: the
+ * workspace is a static device array inside the library (8.4 MB per device,
+ * held until the process exits).  Limit: B*H*S_q <= 16384 rows, else
+ * LH_ERR_SHAPE.  The first call on a device looks up that array's address
+ * (cudaGetSymbolAddress) with the device current; make that first call before
+ * any stream capture.  All calls share the array: calls that overlap on the
+ * GPU race with each other. */
+int lh_attn_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                        const void* do_, int B, int H, int S_q, int S_kv, int q_off, int D, float scale,
+                        void* dq, void* dk, void* dv, void* stream);
+
 /* Fan-out of the selected outputs back to base positions (deterministic pull).
  * Replaces _ScatterToBaseAutograd.forward + _scatter_fanout_fwd_kernel
  * (SEL:408-459, 517-550): item s at pyramid level l with level-local position

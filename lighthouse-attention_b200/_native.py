@@ -40,6 +40,7 @@ _SIGS = {
     "lh_attn_bwd_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 5),
     "lh_attn_bwd": (ctypes.c_int, [_VP] * 6 + [ctypes.c_int] * 6 + [ctypes.c_float] + [_VP] * 4
                     + [ctypes.c_size_t, _VP]),
+    "lh_attn_bwd_noalloc": (ctypes.c_int, [_VP] * 6 + [ctypes.c_int] * 6 + [ctypes.c_float] + [_VP] * 4),
     "lh_scatter_fwd": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
     "lh_scatter_bwd": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
     "lh_unpool_bwd": (ctypes.c_int, [_VP] * 4 + [ctypes.c_int] * 8 + [_VP] * 4),

@@ -24,6 +24,8 @@
 // arrive by TMA (no multicast).  Every mbarrier wait is bounded.
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "lh_common.cuh"
 #include "sm100.cuh"
 
@@ -387,6 +389,74 @@ int attn_bwd(const void* q, const void* k, const void* v, const void* o, const f
   const long long n8 = (long long)rows * D / 8;
   attn_bwd_post_kernel<<<148 * 8, 256, 0, st>>>(dQacc, (__nv_bfloat16*)dq, scale, n8);
   return check_launch("attn_bwd_post_kernel");
+}
+
+}  // namespace lh
+
+namespace lh {
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the attention backward.
+//
+// Some callers cannot allocate device memory at the point where they run the
+// backward: a host runtime that hands the library only the tensors of the
+// step (a JNI / cgo / C++ caller without access to PyTorch's caching
+// allocator, for which cudaMalloc would also synchronise the device in the
+// middle of a step), or a process whose memory pool is reserved up front and
+// forbids new device allocations.  lh_attn_bwd_noalloc serves them: its
+// workspace (the fp32 dQ accumulator and the per-row Delta) lives in the
+// file-scope array below, which the CUDA runtime creates when the library is
+// loaded on a device and keeps until the process exits.
+//
+// Limit: B*H*S_q <= kNoAllocMaxRows rows (8.4 MB per device).  Every call
+// shares the array and it keeps the previous call's contents; the prep kernel
+// rewrites all of it that a call reads (dQacc is zeroed, Delta recomputed).
+// Calls that overlap on the GPU (different streams, or different threads
+// without ordering) race on the array.
+constexpr long long kNoAllocMaxRows = 16384;
+constexpr size_t kNoAllocBytes = (size_t)kNoAllocMaxRows * 128 * sizeof(float) +
+                                 (size_t)kNoAllocMaxRows * sizeof(float);
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+// Device address of g_noalloc_scratch, looked up once per device (with that
+// device current) on the first call made on it.
+static void* noalloc_scratch_ptr(int* rc) {
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("attn_bwd_noalloc: no usable CUDA device");
+    *rc = LH_ERR_LAUNCH;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("attn_bwd_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      *rc = LH_ERR_LAUNCH;
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *rc = LH_OK;
+  return ptrs[dev];
+}
+
+int attn_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const float* lse, const void* dO,
+                     int B, int H, int S_q, int S_kv, int q_off, int D, float scale, void* dq, void* dk, void* dv,
+                     cudaStream_t st) {
+  if ((long long)B * H * S_q > kNoAllocMaxRows) {
+    set_error("attn_bwd_noalloc: B*H*S_q = %lld rows exceeds the static workspace limit of %lld rows",
+              (long long)B * H * S_q, kNoAllocMaxRows);
+    return LH_ERR_SHAPE;
+  }
+  int rc = LH_OK;
+  void* ws = noalloc_scratch_ptr(&rc);
+  if (rc) return rc;
+  // The workspace layout of attn_bwd: dQacc (rows x 128 fp32) then Delta, each 256-byte aligned.
+  return attn_bwd(q, k, v, o, lse, dO, B, H, S_q, S_kv, q_off, D, scale, dq, dk, dv, ws, kNoAllocBytes, st);
 }
 
 }  // namespace lh

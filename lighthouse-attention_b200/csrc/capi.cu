@@ -61,6 +61,8 @@ int attn_fwd(const void*, const void*, const void*, int, int, int, int, int, int
              cudaStream_t);
 size_t attn_bwd_workspace_size(int, int, int, int, int);
 int attn_status(int reset);
+int attn_bwd_noalloc(const void*, const void*, const void*, const void*, const float*, const void*, int, int, int,
+                     int, int, int, float, void*, void*, void*, cudaStream_t);
 int attn_bwd(const void*, const void*, const void*, const void*, const float*, const void*, int, int, int, int,
              int, int, float, void*, void*, void*, void*, size_t, cudaStream_t);
 
@@ -162,6 +164,17 @@ int lh_attn_bwd(const void* q, const void* k, const void* v, const void* o, cons
   LH_REQUIRE(ws && ((uintptr_t)ws & 255) == 0, LH_ERR_ARG, "attn_bwd: workspace must be 256-byte aligned");
   LH_ARCH();
   return attn_bwd(q, k, v, o, lse, dO, B, H, S_q, S_kv, q_off, D, scale, dq, dk, dv, ws, ws_bytes, S_(stream));
+}
+
+int lh_attn_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                        const void* dO, int B, int H, int S_q, int S_kv, int q_off, int D, float scale, void* dq,
+                        void* dk, void* dv, void* stream) {
+  g_err[0] = 0;
+  LH_REQUIRE(q && k && v && o && lse && dO && dq && dk && dv, LH_ERR_ARG, "attn_bwd_noalloc: null pointer");
+  LH_REQUIRE(D == 128, LH_ERR_SHAPE, "attn_bwd_noalloc: head dim must be 128, got %d", D);
+  LH_REQUIRE(B > 0 && H > 0 && S_q > 0 && S_kv > 0 && q_off >= 0, LH_ERR_SHAPE, "attn_bwd_noalloc: bad shape");
+  LH_ARCH();
+  return attn_bwd_noalloc(q, k, v, o, lse, dO, B, H, S_q, S_kv, q_off, D, scale, dq, dk, dv, S_(stream));
 }
 
 int lh_scatter_fwd(const void* attn, const int32_t* inverse, int dtype, int B, int H, int S_sel, int D,

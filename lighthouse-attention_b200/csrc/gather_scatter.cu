@@ -16,23 +16,23 @@ __global__ void __launch_bounds__(kRowThreads)
 gather_kernel(const T* __restrict__ raw0, const T* __restrict__ raw1, const T* __restrict__ raw2,
               const T* __restrict__ pool0, const T* __restrict__ pool1, const T* __restrict__ pool2,
               T* __restrict__ out0, T* __restrict__ out1, T* __restrict__ out2,
-              const int32_t* __restrict__ indices, int H, int S, int D, int S_pool, int S_sel,
-              long long n_chunks) {
+              const int32_t* __restrict__ indices, FastDiv fd_ssel, FastDiv fd_h, int S, int D, int S_pool,
+              int cpr_shift, uint32_t n_chunks) {
   constexpr int VEC = Vec16<T>::N;
-  const int cpr = D / VEC;
   const T* raw = blockIdx.y == 0 ? raw0 : (blockIdx.y == 1 ? raw1 : raw2);
   const T* pool = blockIdx.y == 0 ? pool0 : (blockIdx.y == 1 ? pool1 : pool2);
   T* out = blockIdx.y == 0 ? out0 : (blockIdx.y == 1 ? out1 : out2);
   if (out == nullptr) return;
-  for (long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x; gid < n_chunks;
-       gid += (long long)gridDim.x * blockDim.x) {
-    const long long row = gid / cpr;         // bh * S_sel + s
-    const int c = (int)(gid % cpr) * VEC;
-    const int bh = (int)(row / S_sel);
+  const int H = (int)fd_h.d;
+  for (uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x; gid < n_chunks; gid += gridDim.x * blockDim.x) {
+    const uint32_t row = gid >> cpr_shift;           // bh * S_sel + s
+    const int c = (int)(gid & ((1u << cpr_shift) - 1)) * VEC;
+    const uint32_t bh = fd_ssel.div(row);
     const int idx = __ldg(indices + row);
     const T* src;
     if (idx < S) {
-      const int b = bh / H, h = bh % H;
+      uint32_t b, h;
+      fd_h.divmod(bh, b, h);
       src = raw + (((size_t)b * S + idx) * H + h) * D;
     } else {
       src = pool + ((size_t)bh * S_pool + (idx - S)) * D;
@@ -46,23 +46,22 @@ gather_kernel(const T* __restrict__ raw0, const T* __restrict__ raw1, const T* _
 // window [j*f + f - 1, j*f + 2f - 1) contains t (reference :408-459).
 template <class T>
 __global__ void __launch_bounds__(kRowThreads)
-scatter_fwd_kernel(const T* __restrict__ attn, const int32_t* __restrict__ inverse, Pyramid pyr,
-                   int D, int S_sel, int N_total, T* __restrict__ out, long long n_chunks) {
+scatter_fwd_kernel(const T* __restrict__ attn, const int32_t* __restrict__ inverse, Pyramid pyr, int p_shift,
+                   int D, int S_sel, FastDiv fd_n, T* __restrict__ out, int cpr_shift, uint32_t n_chunks) {
   constexpr int VEC = Vec16<T>::N;
-  const int cpr = D / VEC;
-  for (long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x; gid < n_chunks;
-       gid += (long long)gridDim.x * blockDim.x) {
-    const long long row = gid / cpr;        // bh * N_total + t
-    const int c = (int)(gid % cpr) * VEC;
-    const int bh = (int)(row / N_total);
-    const int t = (int)(row % N_total);
+  for (uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x; gid < n_chunks; gid += gridDim.x * blockDim.x) {
+    const uint32_t row = gid >> cpr_shift;          // bh * N_total + t
+    const int c = (int)(gid & ((1u << cpr_shift) - 1)) * VEC;
+    uint32_t bh, t;
+    fd_n.divmod(row, bh, t);
     const int32_t* inv = inverse + (size_t)bh * pyr.total;
     float acc[VEC];
 #pragma unroll
     for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
-    int f = 1;
-    for (int l = 0; l < pyr.L; ++l, f *= pyr.p) {
-      const int j = (t + 1) / f - 1;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+      if (l >= pyr.L) break;
+      const int j = (int)((t + 1) >> (l * p_shift)) - 1;
       if (j >= 0 && j < pyr.len[l]) {
         const int slot = __ldg(inv + pyr.off[l] + j);
         if (slot >= 0) {
@@ -81,28 +80,28 @@ scatter_fwd_kernel(const T* __restrict__ attn, const int32_t* __restrict__ inver
 // dattn[bh, s] = sum over the item's window of dout[bh, pos] (reference :462-514)
 template <class T>
 __global__ void __launch_bounds__(kRowThreads)
-scatter_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ indices, Pyramid pyr,
-                   int D, int S_sel, int N_total, T* __restrict__ dattn, long long n_chunks) {
+scatter_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ indices, Pyramid pyr, int p_shift,
+                   int D, FastDiv fd_ssel, int N_total, T* __restrict__ dattn, int cpr_shift, uint32_t n_chunks) {
   constexpr int VEC = Vec16<T>::N;
-  const int cpr = D / VEC;
-  for (long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x; gid < n_chunks;
-       gid += (long long)gridDim.x * blockDim.x) {
-    const long long row = gid / cpr;        // bh * S_sel + s
-    const int c = (int)(gid % cpr) * VEC;
-    const int bh = (int)(row / S_sel);
+  for (uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x; gid < n_chunks; gid += gridDim.x * blockDim.x) {
+    const uint32_t row = gid >> cpr_shift;          // bh * S_sel + s
+    const int c = (int)(gid & ((1u << cpr_shift) - 1)) * VEC;
+    const uint32_t bh = fd_ssel.div(row);
     const int idx = __ldg(indices + row);
     float acc[VEC];
 #pragma unroll
     for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
     if (idx >= 0) {
-      int l = 0, f = 1;
-      while (l + 1 < pyr.L && idx >= pyr.off[l + 1]) { ++l; f *= pyr.p; }
-      if (idx < pyr.off[l] + pyr.len[l]) {
-        const int first = (idx - pyr.off[l]) * f + f - 1;
+      int l = 0, lvl_off = 0, lvl_len = pyr.len[0];
+#pragma unroll
+      for (int m = 1; m < 8; ++m)
+        if (m < pyr.L && idx >= pyr.off[m]) { l = m; lvl_off = pyr.off[m]; lvl_len = pyr.len[m]; }
+      if (idx < lvl_off + lvl_len) {
+        const int f = 1 << (l * p_shift);
+        const int first = (idx - lvl_off) * f + f - 1;
+        const int last = min(first + f, N_total);
         const T* src = dout + (size_t)bh * N_total * D + c;
-        for (int i = 0; i < f; ++i) {
-          const int pos = first + i;
-          if (pos >= N_total) break;
+        for (int pos = first; pos < last; ++pos) {
           float v[VEC];
           load16(src + (size_t)pos * D, v);
 #pragma unroll
@@ -132,36 +131,34 @@ template <class T>
 __global__ void __launch_bounds__(kRowThreads)
 unpool_bwd_kernel(const T* __restrict__ d0, const T* __restrict__ d1, const T* __restrict__ d2,
                   T* __restrict__ o0, T* __restrict__ o1, T* __restrict__ o2,
-                  const int32_t* __restrict__ inverse, Pyramid pyr, int H, int D, int S_sel,
-                  long long n_chunks) {
+                  const int32_t* __restrict__ inverse, Pyramid pyr, int p_shift, FastDiv fd_h, FastDiv fd_s,
+                  int D, int S_sel, int cpr_shift, uint32_t n_chunks) {
   constexpr int VEC = Vec16<T>::N;
-  const int cpr = D / VEC;
   const T* dsel = blockIdx.y == 0 ? d0 : (blockIdx.y == 1 ? d1 : d2);
   T* dx = blockIdx.y == 0 ? o0 : (blockIdx.y == 1 ? o1 : o2);
   if (dx == nullptr) return;
-  const int S = pyr.N;
-  for (long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x; gid < n_chunks;
-       gid += (long long)gridDim.x * blockDim.x) {
-    const long long row = gid / cpr;        // (b * S + t) * H + h
-    const int c = (int)(gid % cpr) * VEC;
-    const int h = (int)(row % H);
-    const long long bt = row / H;
-    const int t = (int)(bt % S);
-    const int b = (int)(bt / S);
-    const int bh = b * H + h;
+  const int H = (int)fd_h.d;
+  for (uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x; gid < n_chunks; gid += gridDim.x * blockDim.x) {
+    const uint32_t row = gid >> cpr_shift;          // (b * S + t) * H + h
+    const int c = (int)(gid & ((1u << cpr_shift) - 1)) * VEC;
+    uint32_t bt, h, b, t;
+    fd_h.divmod(row, bt, h);
+    fd_s.divmod(bt, b, t);
+    const uint32_t bh = b * H + h;
     const int32_t* inv = inverse + (size_t)bh * pyr.total;
     float acc[VEC];
 #pragma unroll
     for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
-    int f = 1;
-    for (int l = 0; l < pyr.L; ++l, f *= pyr.p) {
-      const int j = t / f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+      if (l >= pyr.L) break;
+      const int j = (int)(t >> (l * p_shift));
       if (j < pyr.len[l]) {
         const int slot = __ldg(inv + pyr.off[l] + j);
         if (slot >= 0) {
           float v[VEC];
           load16(dsel + ((size_t)bh * S_sel + slot) * D + c, v);
-          const float sc = 1.0f / (float)f;
+          const float sc = 1.0f / (float)(1 << (l * p_shift));
 #pragma unroll
           for (int e = 0; e < VEC; ++e) acc[e] = fmaf(v[e], sc, acc[e]);
         }
@@ -179,23 +176,38 @@ static int grid_for(long long n) {
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+static int log2i(int x) { int s = 0; while ((1 << s) < x) ++s; return s; }
+
+// chunks of 16 bytes per row as a shift; rejects totals beyond 31 bits
+static int row_geometry(const char* what, int dtype, int D, long long rows, int* cpr_shift, uint32_t* n) {
+  const int esz = dtype == LH_DTYPE_BF16 ? 2 : 4;
+  const int cpr = D * esz / 16;
+  if ((D * esz) % 16 || (cpr & (cpr - 1))) { set_error("%s: D*elem_size/16 must be a power of two", what); return LH_ERR_ARG; }
+  const long long total = rows * cpr;
+  if (total >= (1LL << 31)) { set_error("%s: tensor too large (%lld 16-byte chunks)", what, total); return LH_ERR_SHAPE; }
+  *cpr_shift = log2i(cpr);
+  *n = (uint32_t)total;
+  return LH_OK;
+}
+
 int gather_selected(const void* qr, const void* kr, const void* vr, const void* qp, const void* kp,
                     const void* vp, int dtype, int B, int S, int H, int D, int S_pool,
                     const int32_t* indices, int S_sel, void* qs, void* ks, void* vs, cudaStream_t st) {
-  const int esz = dtype == LH_DTYPE_BF16 ? 2 : 4;
-  if ((D * esz) % 16) { set_error("gather: D*elem must be a multiple of 16 bytes"); return LH_ERR_ARG; }
   const void* ptrs[] = {qr, kr, vr, qp, kp, vp, qs, ks, vs};
   for (const void* p : ptrs) if (p && !aligned16(p)) { set_error("gather: pointers must be 16-byte aligned"); return LH_ERR_ARG; }
-  const long long n = (long long)B * H * S_sel * (D * esz / 16);
+  int cs; uint32_t n;
+  int rc = row_geometry("gather", dtype, D, (long long)B * H * S_sel, &cs, &n);
+  if (rc) return rc;
   dim3 grid(grid_for(n), 3);
+  FastDiv fs(S_sel), fh(H);
   if (dtype == LH_DTYPE_BF16) {
     using T = __nv_bfloat16;
     gather_kernel<T><<<grid, kRowThreads, 0, st>>>((const T*)qr, (const T*)kr, (const T*)vr, (const T*)qp,
-        (const T*)kp, (const T*)vp, (T*)qs, (T*)ks, (T*)vs, indices, H, S, D, S_pool, S_sel, n);
+        (const T*)kp, (const T*)vp, (T*)qs, (T*)ks, (T*)vs, indices, fs, fh, S, D, S_pool, cs, n);
   } else {
     using T = float;
     gather_kernel<T><<<grid, kRowThreads, 0, st>>>((const T*)qr, (const T*)kr, (const T*)vr, (const T*)qp,
-        (const T*)kp, (const T*)vp, (T*)qs, (T*)ks, (T*)vs, indices, H, S, D, S_pool, S_sel, n);
+        (const T*)kp, (const T*)vp, (T*)qs, (T*)ks, (T*)vs, indices, fs, fh, S, D, S_pool, cs, n);
   }
   return check_launch("gather_kernel");
 }
@@ -203,26 +215,30 @@ int gather_selected(const void* qr, const void* kr, const void* vr, const void* 
 int scatter_fwd(const void* attn, const int32_t* inverse, int dtype, int B, int H, int S_sel, int D,
                 int N_shard, int N_total, int L, int p, void* out, cudaStream_t st) {
   Pyramid pyr; pyr.init(N_shard, L, p);
-  const int esz = dtype == LH_DTYPE_BF16 ? 2 : 4;
-  if (!aligned16(attn) || !aligned16(out) || (D * esz) % 16) { set_error("scatter_fwd: alignment"); return LH_ERR_ARG; }
-  const long long n = (long long)B * H * N_total * (D * esz / 16);
+  if (!aligned16(attn) || !aligned16(out)) { set_error("scatter_fwd: pointers must be 16-byte aligned"); return LH_ERR_ARG; }
+  int cs; uint32_t n;
+  int rc = row_geometry("scatter_fwd", dtype, D, (long long)B * H * N_total, &cs, &n);
+  if (rc) return rc;
+  FastDiv fn(N_total);
   if (dtype == LH_DTYPE_BF16)
-    scatter_fwd_kernel<__nv_bfloat16><<<grid_for(n), kRowThreads, 0, st>>>((const __nv_bfloat16*)attn, inverse, pyr, D, S_sel, N_total, (__nv_bfloat16*)out, n);
+    scatter_fwd_kernel<__nv_bfloat16><<<grid_for(n), kRowThreads, 0, st>>>((const __nv_bfloat16*)attn, inverse, pyr, log2i(p), D, S_sel, fn, (__nv_bfloat16*)out, cs, n);
   else
-    scatter_fwd_kernel<float><<<grid_for(n), kRowThreads, 0, st>>>((const float*)attn, inverse, pyr, D, S_sel, N_total, (float*)out, n);
+    scatter_fwd_kernel<float><<<grid_for(n), kRowThreads, 0, st>>>((const float*)attn, inverse, pyr, log2i(p), D, S_sel, fn, (float*)out, cs, n);
   return check_launch("scatter_fwd_kernel");
 }
 
 int scatter_bwd(const void* dout, const int32_t* indices, int dtype, int B, int H, int S_sel, int D,
                 int N_shard, int N_total, int L, int p, void* dattn, cudaStream_t st) {
   Pyramid pyr; pyr.init(N_shard, L, p);
-  const int esz = dtype == LH_DTYPE_BF16 ? 2 : 4;
-  if (!aligned16(dout) || !aligned16(dattn) || (D * esz) % 16) { set_error("scatter_bwd: alignment"); return LH_ERR_ARG; }
-  const long long n = (long long)B * H * S_sel * (D * esz / 16);
+  if (!aligned16(dout) || !aligned16(dattn)) { set_error("scatter_bwd: pointers must be 16-byte aligned"); return LH_ERR_ARG; }
+  int cs; uint32_t n;
+  int rc = row_geometry("scatter_bwd", dtype, D, (long long)B * H * S_sel, &cs, &n);
+  if (rc) return rc;
+  FastDiv fs(S_sel);
   if (dtype == LH_DTYPE_BF16)
-    scatter_bwd_kernel<__nv_bfloat16><<<grid_for(n), kRowThreads, 0, st>>>((const __nv_bfloat16*)dout, indices, pyr, D, S_sel, N_total, (__nv_bfloat16*)dattn, n);
+    scatter_bwd_kernel<__nv_bfloat16><<<grid_for(n), kRowThreads, 0, st>>>((const __nv_bfloat16*)dout, indices, pyr, log2i(p), D, fs, N_total, (__nv_bfloat16*)dattn, cs, n);
   else
-    scatter_bwd_kernel<float><<<grid_for(n), kRowThreads, 0, st>>>((const float*)dout, indices, pyr, D, S_sel, N_total, (float*)dattn, n);
+    scatter_bwd_kernel<float><<<grid_for(n), kRowThreads, 0, st>>>((const float*)dout, indices, pyr, log2i(p), D, fs, N_total, (float*)dattn, cs, n);
   return check_launch("scatter_bwd_kernel");
 }
 
@@ -237,16 +253,19 @@ int build_inverse(const int32_t* indices, int B, int H, int S_sel, int S_tot, in
 int unpool_bwd(const void* dq, const void* dk, const void* dv, const int32_t* inverse, int dtype, int B,
                int S, int H, int D, int L, int p, int S_sel, void* dxq, void* dxk, void* dxv, cudaStream_t st) {
   Pyramid pyr; pyr.init(S, L, p);
-  const int esz = dtype == LH_DTYPE_BF16 ? 2 : 4;
-  if ((D * esz) % 16) { set_error("unpool_bwd: D*elem must be a multiple of 16 bytes"); return LH_ERR_ARG; }
-  const long long n = (long long)B * S * H * (D * esz / 16);
+  const void* ptrs[] = {dq, dk, dv, dxq, dxk, dxv};
+  for (const void* q : ptrs) if (q && !aligned16(q)) { set_error("unpool_bwd: pointers must be 16-byte aligned"); return LH_ERR_ARG; }
+  int cs; uint32_t n;
+  int rc = row_geometry("unpool_bwd", dtype, D, (long long)B * S * H, &cs, &n);
+  if (rc) return rc;
   dim3 grid(grid_for(n), 3);
+  FastDiv fh(H), fs(S);
   if (dtype == LH_DTYPE_BF16) {
     using T = __nv_bfloat16;
-    unpool_bwd_kernel<T><<<grid, kRowThreads, 0, st>>>((const T*)dq, (const T*)dk, (const T*)dv, (T*)dxq, (T*)dxk, (T*)dxv, inverse, pyr, H, D, S_sel, n);
+    unpool_bwd_kernel<T><<<grid, kRowThreads, 0, st>>>((const T*)dq, (const T*)dk, (const T*)dv, (T*)dxq, (T*)dxk, (T*)dxv, inverse, pyr, log2i(p), fh, fs, D, S_sel, cs, n);
   } else {
     using T = float;
-    unpool_bwd_kernel<T><<<grid, kRowThreads, 0, st>>>((const T*)dq, (const T*)dk, (const T*)dv, (T*)dxq, (T*)dxk, (T*)dxv, inverse, pyr, H, D, S_sel, n);
+    unpool_bwd_kernel<T><<<grid, kRowThreads, 0, st>>>((const T*)dq, (const T*)dk, (const T*)dv, (T*)dxq, (T*)dxk, (T*)dxv, inverse, pyr, log2i(p), fh, fs, D, S_sel, cs, n);
   }
   return check_launch("unpool_bwd_kernel");
 }

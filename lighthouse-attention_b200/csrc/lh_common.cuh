@@ -52,6 +52,33 @@ __host__ __device__ inline long long sel_len(long long N, int L, int p, int k) {
   return t;
 }
 
+// Division of non-negative 31-bit integers by a launch-invariant divisor with
+// one multiply-high, an add and a shift (Granlund & Montgomery, "Division by
+// invariant integers using multiplication", PLDI 1994): with s = ceil(log2 d)
+// and m = floor(2^32 (2^s - d) / d) + 1, n / d = (umulhi(n, m) + n) >> s for
+// 0 <= n < 2^31.  Built on the host, used in row-mover index arithmetic.
+struct FastDiv {
+  uint32_t d, m, s;
+  __host__ __device__ FastDiv() : d(1), m(0), s(0) {}
+  __host__ explicit FastDiv(uint32_t div) : d(div) {
+    s = 0;
+    while ((1ull << s) < div) ++s;
+    m = (uint32_t)((((1ull << s) - div) << 32) / div + 1);
+  }
+  __host__ __device__ __forceinline__ uint32_t div(uint32_t n) const {
+#ifdef __CUDA_ARCH__
+    const uint32_t hi = __umulhi(n, m);
+#else
+    const uint32_t hi = (uint32_t)(((uint64_t)n * m) >> 32);
+#endif
+    return (hi + n) >> s;
+  }
+  __host__ __device__ __forceinline__ void divmod(uint32_t n, uint32_t& q, uint32_t& r) const {
+    q = div(n);
+    r = n - q * d;
+  }
+};
+
 template <class T> struct Vec16;
 template <> struct Vec16<__nv_bfloat16> { static constexpr int N = 8; };
 template <> struct Vec16<float> { static constexpr int N = 4; };

@@ -19,6 +19,10 @@ namespace lh {
 
 constexpr int kPyrThreads = 128;
 
+// blockIdx.z selects the tensor (0 = q, 1 = k, 2 = v): each thread carries the
+// level accumulators of one tensor only, and q / k threads also produce that
+// tensor's norm scores.  Loads are double-buffered: the next U tokens are in
+// flight while the current ones are reduced.
 template <class T, int D, int LV>
 __global__ void __launch_bounds__(kPyrThreads)
 pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T* __restrict__ xv,
@@ -27,8 +31,14 @@ pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T
                      float* __restrict__ sqk, float* __restrict__ skq, Pyramid pyr, int S_pool) {
   constexpr int VEC = Vec16<T>::N;       // elements per 16-byte chunk
   constexpr int LPH = D / VEC;           // lanes per head row
+  constexpr int U = 4;                   // tokens per load batch
   static_assert(LPH <= 32 && (32 % LPH) == 0, "head row must fit a warp segment");
-  extern __shared__ float s_scores[];    // [2][H][tpc_tot]
+  extern __shared__ float s_scores[];    // [H][tpc_tot]
+  const int which = blockIdx.z;
+  const T* x = which == 0 ? xq : (which == 1 ? xk : xv);
+  T* px = which == 0 ? pq : (which == 1 ? pk : pv);
+  float* sc = which == 0 ? sqk : skq;
+  const bool scored = which < 2;
   const int b = blockIdx.y;
   const int t0 = blockIdx.x * tpc;
   const int ntok = min(tpc, S - t0);
@@ -36,8 +46,6 @@ pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T
   int lvl_base[LV];
 #pragma unroll
   for (int l = 0; l < LV; ++l) { lvl_base[l] = tpc_tot; tpc_tot += tpc >> (l * p_shift); }
-  float* sb_q = s_scores;
-  float* sb_k = s_scores + H * tpc_tot;
 
   const int pairs = H * LPH;
   const int pairs_padded = (pairs + 31) & ~31;
@@ -45,77 +53,81 @@ pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T
     const bool active = pr < pairs;
     const int h = active ? pr / LPH : 0;
     const int c = (pr % LPH) * VEC;
-    const size_t row0 = ((size_t)b * S + t0) * H + h;     // (b, t0, h) row
-    float acc_q[LV][VEC], acc_k[LV][VEC], acc_v[LV][VEC];
-    float mx_q[LV], mx_k[LV];
+    const T* src = x + (((size_t)b * S + t0) * H + h) * D + c;
+    const size_t tok_stride = (size_t)H * D;
+    float acc[LV][VEC];
+    float mx[LV];
 #pragma unroll
     for (int l = 1; l < LV; ++l) {
-      mx_q[l] = -INFINITY; mx_k[l] = -INFINITY;
+      mx[l] = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) acc_q[l][e] = acc_k[l][e] = acc_v[l][e] = 0.f;
+      for (int e = 0; e < VEC; ++e) acc[l][e] = 0.f;
     }
-    constexpr int U = 4;  // tokens in flight per thread
-    for (int i0 = 0; i0 < ntok; i0 += U) {
-      float fq[U][VEC], fk[U][VEC], fv[U][VEC];
+    float buf[2][U][VEC];
+    auto load_batch = [&](int slot, int i0) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        if (active && i0 + u < ntok) {
-          const size_t off = (row0 + (size_t)(i0 + u) * H) * D + c;
-          load16(xq + off, fq[u]); load16(xk + off, fk[u]); load16(xv + off, fv[u]);
-        } else {
+        if (active && i0 + u < ntok) load16(src + (size_t)(i0 + u) * tok_stride, buf[slot][u]);
+        else {
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) fq[u][e] = fk[u][e] = fv[u][e] = 0.f;
+          for (int e = 0; e < VEC; ++e) buf[slot][u][e] = 0.f;
         }
       }
+    };
+    auto process = [&](int slot, int i0) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int i = i0 + u;
-        float ssq = 0.f, ssk = 0.f;
+        float nrm = 0.f;
+        if (scored) {
+          float ss = 0.f;
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) { ssq = fmaf(fq[u][e], fq[u][e], ssq); ssk = fmaf(fk[u][e], fk[u][e], ssk); }
+          for (int e = 0; e < VEC; ++e) ss = fmaf(buf[slot][u][e], buf[slot][u][e], ss);
 #pragma unroll
-        for (int m = LPH / 2; m > 0; m >>= 1) {
-          ssq += __shfl_xor_sync(0xffffffffu, ssq, m, LPH);
-          ssk += __shfl_xor_sync(0xffffffffu, ssk, m, LPH);
+          for (int m = LPH / 2; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m, LPH);
+          nrm = round_to(sqrtf(ss), (const T*)nullptr);
         }
         if (i >= ntok || !active) continue;
-        const float nq = round_to(sqrtf(ssq), (const T*)nullptr);
-        const float nk = round_to(sqrtf(ssk), (const T*)nullptr);
-        if (c == 0) { sb_q[h * tpc_tot + i] = nq; sb_k[h * tpc_tot + i] = nk; }
+        if (scored && c == 0) s_scores[h * tpc_tot + i] = nrm;
 #pragma unroll
         for (int l = 1; l < LV; ++l) {
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) { acc_q[l][e] += fq[u][e]; acc_k[l][e] += fk[u][e]; acc_v[l][e] += fv[u][e]; }
-          mx_q[l] = fmaxf(mx_q[l], nq); mx_k[l] = fmaxf(mx_k[l], nk);
+          for (int e = 0; e < VEC; ++e) acc[l][e] += buf[slot][u][e];
+          mx[l] = fmaxf(mx[l], nrm);
           const int sh = l * p_shift;
           if (((i + 1) & ((1 << sh) - 1)) == 0) {
             const int j = i >> sh;                              // pooled index inside this CTA
             const float inv = 1.0f / (float)(1 << sh);          // exact: power of two
-            float oq[VEC], ok[VEC], ov[VEC];
+            float o[VEC];
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) { oq[e] = acc_q[l][e] * inv; ok[e] = acc_k[l][e] * inv; ov[e] = acc_v[l][e] * inv;
-                                            acc_q[l][e] = acc_k[l][e] = acc_v[l][e] = 0.f; }
+            for (int e = 0; e < VEC; ++e) { o[e] = acc[l][e] * inv; acc[l][e] = 0.f; }
             const size_t prow = ((size_t)b * H + h) * S_pool + (pyr.off[l] - S) + (t0 >> sh) + j;
-            store16(pq + prow * D + c, oq); store16(pk + prow * D + c, ok); store16(pv + prow * D + c, ov);
-            if (c == 0) { sb_q[h * tpc_tot + lvl_base[l] + j] = mx_q[l]; sb_k[h * tpc_tot + lvl_base[l] + j] = mx_k[l]; }
-            mx_q[l] = -INFINITY; mx_k[l] = -INFINITY;
+            store16(px + prow * D + c, o);
+            if (scored && c == 0) s_scores[h * tpc_tot + lvl_base[l] + j] = mx[l];
+            mx[l] = -INFINITY;
           }
         }
       }
+    };
+    // two batches per trip so that the buffer index is a compile-time constant
+    load_batch(0, 0);
+    for (int i0 = 0; i0 < ntok; i0 += 2 * U) {
+      if (i0 + U < ntok) load_batch(1, i0 + U);
+      process(0, i0);
+      if (i0 + U >= ntok) break;
+      if (i0 + 2 * U < ntok) load_batch(0, i0 + 2 * U);
+      process(1, i0 + U);
     }
   }
+  if (!scored) return;
   __syncthreads();
   // Contiguous per-(head, level) runs of fp32 scores.
   for (int h = 0; h < H; ++h) {
 #pragma unroll
     for (int l = 0; l < LV; ++l) {
       const int n = ntok >> (l * p_shift);
-      float* gq = sqk + ((size_t)b * H + h) * pyr.total + pyr.off[l] + (t0 >> (l * p_shift));
-      float* gk = skq + ((size_t)b * H + h) * pyr.total + pyr.off[l] + (t0 >> (l * p_shift));
-      for (int j = threadIdx.x; j < n; j += blockDim.x) {
-        gq[j] = sb_q[h * tpc_tot + lvl_base[l] + j];
-        gk[j] = sb_k[h * tpc_tot + lvl_base[l] + j];
-      }
+      float* g = sc + ((size_t)b * H + h) * pyr.total + pyr.off[l] + (t0 >> (l * p_shift));
+      for (int j = threadIdx.x; j < n; j += blockDim.x) g[j] = s_scores[h * tpc_tot + lvl_base[l] + j];
     }
   }
 }
@@ -131,11 +143,11 @@ static int launch_pyr(const void* xq, const void* xk, const void* xv, int B, int
   const int S_pool = pyr.total - S;
   int tpc_tot = 0;
   for (int l = 0; l < LV; ++l) tpc_tot += tpc >> (l * shift);
-  const size_t smem = (size_t)2 * H * tpc_tot * sizeof(float);
+  const size_t smem = (size_t)H * tpc_tot * sizeof(float);
   if (smem > 200 * 1024) { set_error("pyramid: H*tpc too large for shared memory"); return LH_ERR_SHAPE; }
   auto kern = pyramid_score_kernel<T, D, LV>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dim3 grid((S + tpc - 1) / tpc, B);
+  dim3 grid((S + tpc - 1) / tpc, B, 3);
   kern<<<grid, kPyrThreads, smem, st>>>((const T*)xq, (const T*)xk, (const T*)xv, S, H, shift, tpc,
                                         (T*)pq, (T*)pk, (T*)pv, sqk, skq, pyr, S_pool);
   return check_launch("pyramid_score_kernel");

@@ -70,13 +70,34 @@ __device__ __forceinline__ void bitonic_stage(int k, int j, int lane, float (&ke
   }
 }
 
+// The (k, j) stage sequence is expanded at compile time so that every
+// register index and direction test in bitonic_stage is a constant.
+template <int NP, int K, int J>
+struct BitonicStages {
+  static __device__ __forceinline__ void run(int lane, float (&key)[4], float (&pf)[4], int (&ix)[4]) {
+    bitonic_stage<NP>(K, J, lane, key, pf, ix);
+    BitonicStages<NP, K, J / 2>::run(lane, key, pf, ix);
+  }
+};
+template <int NP, int K>
+struct BitonicStages<NP, K, 0> {
+  static __device__ __forceinline__ void run(int, float (&)[4], float (&)[4], int (&)[4]) {}
+};
+template <int NP, int K>
+struct BitonicNet {
+  static __device__ __forceinline__ void run(int lane, float (&key)[4], float (&pf)[4], int (&ix)[4]) {
+    BitonicNet<NP, K / 2>::run(lane, key, pf, ix);
+    BitonicStages<NP, K, K / 2>::run(lane, key, pf, ix);
+  }
+};
+template <int NP>
+struct BitonicNet<NP, 1> {
+  static __device__ __forceinline__ void run(int, float (&)[4], float (&)[4], int (&)[4]) {}
+};
+
 template <int NP>
 __device__ __forceinline__ void bitonic128(int lane, float (&key)[4], float (&pf)[4], int (&ix)[4]) {
-#pragma unroll
-  for (int k = 2; k <= kSelTopk; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) bitonic_stage<NP>(k, j, lane, key, pf, ix);
-  }
+  BitonicNet<NP, kSelTopk>::run(lane, key, pf, ix);
 }
 
 struct SelGeom {
@@ -86,11 +107,12 @@ struct SelGeom {
 };
 
 // Reference level `lev` (1 = raw tokens, L = coarsest) is pyramid level lev-1.
-__device__ __forceinline__ bool refined(const uint32_t* bm, const SelGeom& g, int lev, int idx, int tile) {
+__device__ __forceinline__ bool refined(const uint32_t* bm, const int* bm_off, const SelGeom& g, int lev, int idx,
+                                        int tile) {
   if (lev < 2) return false;
   const int start = tile * (g.ncc << ((g.L - lev) * g.shift));
   const int rel = idx - start;
-  return (bm[g.bm_word_off[lev] + (rel >> 5)] >> (rel & 31)) & 1u;
+  return (bm[bm_off[lev] + (rel >> 5)] >> (rel & 31)) & 1u;
 }
 
 __global__ void __launch_bounds__(32)
@@ -98,7 +120,9 @@ select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ s
                    Pyramid pyr, int32_t* __restrict__ indices, int32_t* __restrict__ inverse) {
   extern __shared__ uint32_t s_dyn[];
   int* s_parent = reinterpret_cast<int*>(s_dyn);            // [128]
-  uint32_t* s_bm = s_dyn + kSelTopk;                        // refinement bitmaps
+  int* s_bmoff = reinterpret_cast<int*>(s_dyn + kSelTopk);  // [8] bitmap word offset per level
+  int* s_lvloff = s_bmoff + 8;                              // [8] pyramid offset per level
+  uint32_t* s_bm = s_dyn + kSelTopk + 16;                   // refinement bitmaps
   const int lane = threadIdx.x;
   const int bh = blockIdx.x / g.T;
   const int tile = blockIdx.x % g.T;
@@ -106,12 +130,13 @@ select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ s
   const float* sk = sk_all + (size_t)bh * g.S_tot;
   for (int w = lane; w < g.bm_words; w += 32) s_bm[w] = 0u;
   for (int i = lane; i < kSelTopk; i += 32) s_parent[i] = -1;
+  if (lane < 8) { s_bmoff[lane] = g.bm_word_off[lane]; s_lvloff[lane] = pyr.off[lane]; }
   __syncwarp();
 
   const int pmask = g.p - 1;
   for (int lev = g.L; lev >= 2; --lev) {
-    const int lvl_off = pyr.off[lev - 1];
-    const int K_end = pyr.len[lev - 1] - 1;
+    const int lvl_off = s_lvloff[lev - 1];
+    const int K_end = (g.N >> ((lev - 1) * g.shift)) - 1;    // last entry of this level
     const int ncand = (lev == g.L) ? g.ncc : g.p * kSelTopk;
     const int tile_start = tile * g.ncc;
     auto cand = [&](int c) -> int {
@@ -173,29 +198,34 @@ select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ s
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int rel = kept[r] - start;
-      if (kept[r] >= 0) atomicOr(&s_bm[g.bm_word_off[lev] + (rel >> 5)], 1u << (rel & 31));
+      if (kept[r] >= 0) atomicOr(&s_bm[s_bmoff[lev] + (rel >> 5)], 1u << (rel & 31));
     }
     __syncwarp();
   }
 
-  // ---- placement: post-order walk of each coarsest entry's refinement tree
+  // ---- placement: post-order walk of each coarsest entry's refinement tree.
+  // Stackless: children of (lev, idx) are (lev-1, idx*p .. idx*p+p-1), so the
+  // walk descends to the first child of refined nodes, steps to the next
+  // sibling, and climbs to (and emits) the parent after its last child.
   const int per_lane = g.ncc / 32;
   const int e0 = tile * g.ncc + lane * per_lane;
-  int count = 0;
-  int st_lev[8], st_idx[8], st_c[8];
-  for (int e = e0; e < e0 + per_lane; ++e) {
-    int d = 0;
-    st_lev[0] = g.L; st_idx[0] = e; st_c[0] = 0;
-    while (d >= 0) {
-      const int lev = st_lev[d], idx = st_idx[d];
-      if (st_c[d] < g.p && refined(s_bm, g, lev, idx, tile)) {
-        const int c = st_c[d]++;
-        ++d; st_lev[d] = lev - 1; st_idx[d] = idx * g.p + c; st_c[d] = 0;
+  auto walk = [&](int e, auto&& visit) {
+    int lev = g.L, idx = e;
+    while (lev >= 2 && refined(s_bm, s_bmoff, g, lev, idx, tile)) { idx <<= g.shift; --lev; }
+    while (true) {
+      visit(lev, idx);
+      if (lev == g.L) break;
+      if ((idx & pmask) != pmask) {
+        ++idx;
+        while (lev >= 2 && refined(s_bm, s_bmoff, g, lev, idx, tile)) { idx <<= g.shift; --lev; }
       } else {
-        ++count; --d;
+        idx >>= g.shift;
+        ++lev;
       }
     }
-  }
+  };
+  int count = 0;
+  for (int e = e0; e < e0 + per_lane; ++e) walk(e, [&](int, int) { ++count; });
   int incl = count;
 #pragma unroll
   for (int m = 1; m < 32; m <<= 1) {
@@ -206,20 +236,12 @@ select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ s
   int32_t* out = indices + (size_t)bh * g.S_sel;
   int32_t* inv = inverse ? inverse + (size_t)bh * g.S_tot : nullptr;
   for (int e = e0; e < e0 + per_lane; ++e) {
-    int d = 0;
-    st_lev[0] = g.L; st_idx[0] = e; st_c[0] = 0;
-    while (d >= 0) {
-      const int lev = st_lev[d], idx = st_idx[d];
-      if (st_c[d] < g.p && refined(s_bm, g, lev, idx, tile)) {
-        const int c = st_c[d]++;
-        ++d; st_lev[d] = lev - 1; st_idx[d] = idx * g.p + c; st_c[d] = 0;
-      } else {
-        const int pidx = idx + pyr.off[lev - 1];
-        out[slot] = pidx;
-        if (inv) inv[pidx] = slot;
-        ++slot; --d;
-      }
-    }
+    walk(e, [&](int lev, int idx) {
+      const int pidx = idx + s_lvloff[lev - 1];
+      out[slot] = pidx;
+      if (inv) inv[pidx] = slot;
+      ++slot;
+    });
   }
 }
 
@@ -259,7 +281,7 @@ int select_topk(const float* sqk, const float* skq, int B, int H, int S, int L, 
   SelGeom g; Pyramid pyr;
   int rc = select_geometry(S, L, p, k, &g, &pyr);
   if (rc) return rc;
-  const size_t smem = (kSelTopk + (size_t)g.bm_words) * sizeof(uint32_t);
+  const size_t smem = (kSelTopk + 16 + (size_t)g.bm_words) * sizeof(uint32_t);
   if (smem > 200 * 1024) { set_error("select: refinement bitmaps exceed shared memory"); return LH_ERR_SHAPE; }
   if (smem > 48 * 1024) cudaFuncSetAttribute(select_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (inverse) {

@@ -17,7 +17,8 @@
 //               dK_j += dS^T Q_i             (SS, TMEM cols 384..511)
 //               dQ_i  = dS K_j               (SS, dS read MN-major; TMEM cols 128..255)
 //             the softmax warps then drain dQ_i from TMEM into the fp32 dQacc
-//             with vector atomics.  At the end dK (times scale) and dV are
+//             with vector atomics.  Eight compute warps: two per TMEM lane
+//             quadrant, each owning 64 of the 128 columns.  At the end dK (times scale) and dV are
 //             written as bf16.
 //   3. post:  dQ = bf16(dQacc * scale)
 // Shared-memory operands use the 128-byte swizzle; Q_i / dO_i / K_j / V_j
@@ -41,7 +42,7 @@ constexpr int kTile = 128;
 constexpr int kD = 128;
 constexpr int kBox = 16384;
 constexpr int kTileBytes = 2 * kBox;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // producer, MMA, 8 compute warps (2 per TMEM lane quadrant)
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384, kTmemCols = 512;
 }  // namespace bwd
 
@@ -97,9 +98,9 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     mbar_init(&sm->q_full, 1);
     mbar_init(&sm->q_empty, 1);
     mbar_init(&sm->s_ready, 1);
-    mbar_init(&sm->p_ready, 128);
+    mbar_init(&sm->p_ready, 256);
     mbar_init(&sm->dq_ready, 1);
-    mbar_init(&sm->dq_free, 128);
+    mbar_init(&sm->dq_free, 256);
     sm->abort = 0;
     fence_mbar_init();
   }
@@ -177,12 +178,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           mma_ss(tbase + kColDK, smem_desc_sw128(adS + off, 16, 1024), smem_desc_sw128(aQ + kk * 2048, kBox, 1024),
                  id_kmn, (t > 0 || kk > 0) ? 1u : 0u);
         }
+        mma_commit(&sm->q_empty);                 // Q_i / dO_i no longer read: fetch the next tile
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)    // dQ_i = dS K   (K = key rows)
           mma_ss(tbase + kColDP, smem_desc_sw128(adS + kk * 2048, kBox, 1024),
                  smem_desc_sw128(aK + kk * 2048, kBox, 1024), id_mnmn, kk > 0);
         mma_commit(&sm->dq_ready);
-        mma_commit(&sm->q_empty);
       }
       __syncwarp();
     }
@@ -190,26 +191,27 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     // ------------------------------------------------------------ softmax / dS / drain
     const int quad = warp & 3;
     const int r = quad * 32 + lane;                 // key row inside the tile (TMEM lane)
-    const int tid = threadIdx.x - 64;               // 0..127
+    const int tid = threadIdx.x - 64;               // 0..255
+    const int g = tid >> 7;                         // column half: query columns / d columns [64g, 64g+64)
     const int kv_pos = j * kTile + r;
     const uint32_t lane_base = tbase + ((uint32_t)(quad * 32) << 16);
     bool ok = true;
     for (int t = 0; t < n_it && ok; ++t) {
       const int i = i0 + t;
       const int buf = t & 1;
-      {
+      if (tid < kTile) {
         const int q = i * kTile + tid;
         sm->lse2[buf][tid] = q < S_q ? LSE[(size_t)bh * S_q + q] * 1.4426950408889634f : INFINITY;
         sm->delta[buf][tid] = q < S_q ? Delta[(size_t)bh * S_q + q] : 0.f;
       }
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 256);
       ok = mbar_wait(&sm->s_ready, t & 1, abort);
       if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
       tc_fence_after();
       const int q_lo = q_off + i * kTile;
       const bool need_mask = (j * kTile + kTile - 1 > q_lo) || (i * kTile + kTile > S_q) || (j * kTile + kTile > S_kv);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {               // 64 query columns per half
+      {
+        const int h = g;                            // this warp's 64 query columns
         uint32_t pk[32];
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2) {
@@ -253,7 +255,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       const int qrow = i * kTile + r;
       float* dst = dQacc + ((size_t)bh * S_q + qrow) * kD;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c2 = 0; c2 < 2; ++c2) {
+        const int c = 2 * g + c2;                   // this warp's 64 d columns
         uint32_t v[32];
         tmem_ld32(lane_base + kColDP + c * 32, v);
         tmem_ld_wait();
@@ -277,7 +280,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const float mul = which == 0 ? 1.0f : scale;
         __nv_bfloat16* row = (which == 0 ? dV : dK) + ((size_t)bh * S_kv + kv_pos) * kD;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c2 = 0; c2 < 2; ++c2) {
+          const int c = 2 * g + c2;
           uint32_t v[32];
           if (n_it > 0) {
             tmem_ld32(lane_base + col + c * 32, v);

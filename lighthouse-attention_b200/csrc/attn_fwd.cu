@@ -3,23 +3,28 @@
 // Replaces F.scaled_dot_product_attention(q, k, v, is_causal=True) on the
 // gathered sequence (reference src/lighthouse_selection.py:815).
 //
-// One CTA per (128-row query tile, b*h), 192 threads, warp-specialised:
-//   warp 0      TMA producer: Q once, then K/V tiles through an NST-stage ring
+// One CTA per (pair of 128-row query tiles A and B, b*h), 384 threads,
+// warp-specialised (warpgroup 0 gives registers to the softmax warpgroups
+// with setmaxnreg: 56 + 2 x 224 per thread-slot = the 3 x 168 of the launch):
+//   warp 0      TMA producer: Q_A and Q_B once, then K/V tiles through a
+//               two-stage ring shared by both query tiles
 //   warp 1      TMEM owner + MMA issuer (one elected lane):
-//                 S_j = Q K_j^T  -> TMEM S[j%2]  (SS MMA, both K-major, SW128)
-//                 O  += P_j V_j  -> TMEM O       (TS MMA: P read from TMEM,
+//                 S_X = Q_X K_j^T  -> TMEM S_X   (SS MMA, both K-major, SW128)
+//                 O_X += P_X V_j   -> TMEM O_X   (TS MMA: P read from TMEM,
 //                                                 V as an MN-major SW128 operand)
-//   warps 2..5  softmax: each thread owns one query row (= TMEM lane), reads
-//               S with tcgen05.ld, keeps the running max / sum in registers,
-//               writes P (bf16) back over its own S columns with tcgen05.st.
-//               O is rescaled in TMEM only when a row max grows by more than
-//               2^8 (the stale max is consistent for numerator and
-//               denominator, so the result is exact up to rounding).
-// S_{j+1} is issued before PV_j so that the tensor core works on the next
-// tile while the softmax warps handle the current one.
+//   warps 4..7  softmax for tile A, warps 8..11 softmax for tile B: each thread
+//               owns one query row (= TMEM lane), reads S with tcgen05.ld,
+//               keeps the running max / sum in registers and writes P (bf16)
+//               back over its own S columns with tcgen05.st.
+// The issue order PV_A(j), S_A(j+1), PV_B(j), S_B(j+1) keeps the tensor core
+// busy with one tile while the other tile's softmax runs.  Because S_X(j+1)
+// is issued after PV_X(j), its completion also means O_X is up to date, so a
+// softmax warp may rescale O_X in TMEM right after S_X(j+1) arrives.  O is
+// rescaled only when a row max grows by more than 2^8 (the stale max is
+// consistent for numerator and denominator).
 //
-// TMEM columns: S[0] 0..127, S[1] 128..255, O 256..383 (512 allocated).
-// Every mbarrier wait is bounded; on timeout the CTA sets *status and leaves.
+// TMEM columns: S_A 0..127, S_B 128..255, O_A 256..383, O_B 384..511.
+// Every mbarrier wait is bounded; on timeout the CTA sets a status flag and leaves.
 #include <cudaTypedefs.h>
 
 #include "lh_common.cuh"
@@ -34,50 +39,56 @@ constexpr int kTile = 128;       // query rows and key rows per tile
 constexpr int kD = 128;          // head dim
 constexpr int kBox = 16384;      // one 128 x 64 bf16 TMA box (128-byte rows)
 constexpr int kTileBytes = 2 * kBox;
-constexpr int kThreads = 192;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256, kTmemCols = 512;
+constexpr int kNst = 2;          // K/V stages
+constexpr int kThreads = 384;   // 3 warpgroups: {producer, MMA, 2 idle}, softmax A, softmax B
+__host__ __device__ constexpr uint32_t col_s(int x) { return x ? 128u : 0u; }
+__host__ __device__ constexpr uint32_t col_o(int x) { return x ? 384u : 256u; }
+constexpr uint32_t kTmemCols = 512;
 }  // namespace fwd
 
 __device__ int g_attn_status;    // set to 1 when a bounded wait gave up
 
-template <int NST>
 struct FwdSmem {
-  uint64_t q_full, o_final;
-  uint64_t k_full[NST], v_full[NST], kv_empty[NST];
-  uint64_t s_full[2], p_full[2], o_done;
+  uint64_t q_full;
+  uint64_t k_full[fwd::kNst], v_full[fwd::kNst], kv_empty[fwd::kNst];
+  uint64_t s_full[2], p_ready[2], o_final[2];
   uint32_t tmem_base;
   int abort;
 };
 
-template <int NST>
 __global__ void __launch_bounds__(fwd::kThreads, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, float* __restrict__ LSE,
-                int S_q, int S_kv, int q_off, int n_qt, float scale2) {
+                int S_q, int S_kv, int q_off, int n_pairs, float scale2) {
   using namespace fwd;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = base;
-  uint8_t* sK = base + kTileBytes;
-  uint8_t* sV = base + kTileBytes * (1 + NST);
-  FwdSmem<NST>* sm = reinterpret_cast<FwdSmem<NST>*>(base + kTileBytes * (1 + 2 * NST));
+  uint8_t* sQ = base;                                  // Q_A, Q_B
+  uint8_t* sK = base + 2 * kTileBytes;
+  uint8_t* sV = base + (2 + kNst) * kTileBytes;
+  FwdSmem* sm = reinterpret_cast<FwdSmem*>(base + (2 + 2 * kNst) * kTileBytes);
 
   const int bh = blockIdx.x;
-  const int qt = n_qt - 1 - blockIdx.y;      // heaviest query tiles first
-  // Causal over global positions: query row r sits at q_off + r, key row c at c.
-  const int q_lo = q_off + qt * kTile;
-  const int q_hi = q_off + min(qt * kTile + kTile, S_q) - 1;
-  const int nkv = min((S_kv + kTile - 1) / kTile, q_hi / kTile + 1);
+  const int pair = n_pairs - 1 - blockIdx.y;           // heaviest query tiles first
+  const int n_qt = (S_q + kTile - 1) / kTile;
+  const int n_kt = (S_kv + kTile - 1) / kTile;
+  int qt[2], nkv[2], q_lo[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    qt[x] = 2 * pair + x;
+    q_lo[x] = q_off + qt[x] * kTile;
+    const int q_hi = q_off + min(qt[x] * kTile + kTile, S_q) - 1;
+    nkv[x] = qt[x] < n_qt ? min(n_kt, q_hi / kTile + 1) : 0;   // causal: key tiles this tile sees
+  }
+  const int nkv_max = max(nkv[0], nkv[1]);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // A CTA of an earlier launch gave up a wait: do nothing until the host resets.
   if (*reinterpret_cast<volatile int*>(&g_attn_status)) return;
 
   if (threadIdx.x == 0) {
     mbar_init(&sm->q_full, 1);
-    mbar_init(&sm->o_final, 1);
-    for (int s = 0; s < NST; ++s) { mbar_init(&sm->k_full[s], 1); mbar_init(&sm->v_full[s], 1); mbar_init(&sm->kv_empty[s], 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&sm->s_full[b], 1); mbar_init(&sm->p_full[b], 128); }
-    mbar_init(&sm->o_done, 1);
+    for (int s = 0; s < kNst; ++s) { mbar_init(&sm->k_full[s], 1); mbar_init(&sm->v_full[s], 1); mbar_init(&sm->kv_empty[s], 1); }
+    for (int x = 0; x < 2; ++x) { mbar_init(&sm->s_full[x], 1); mbar_init(&sm->p_ready[x], 128); mbar_init(&sm->o_final[x], 1); }
     sm->abort = 0;
     fence_mbar_init();
   }
@@ -88,16 +99,24 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tbase = sm->tmem_base;
   volatile int* abort = &sm->abort;
 
+  if (warp < 4) {
+  // Warpgroup 0 hands registers to the softmax warpgroups (one aligned setmaxnreg per warpgroup).
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmK); tma_prefetch_desc(&tmV);
-      mbar_expect_tx(&sm->q_full, kTileBytes);
-      tma_load_3d(sQ, &tmQ, &sm->q_full, 0, qt * kTile, bh);
-      tma_load_3d(sQ + kBox, &tmQ, &sm->q_full, 64, qt * kTile, bh);
+      const bool two = nkv[1] > 0;
+      mbar_expect_tx(&sm->q_full, (two ? 2 : 1) * kTileBytes);
+      tma_load_3d(sQ, &tmQ, &sm->q_full, 0, qt[0] * kTile, bh);
+      tma_load_3d(sQ + kBox, &tmQ, &sm->q_full, 64, qt[0] * kTile, bh);
+      if (two) {
+        tma_load_3d(sQ + kTileBytes, &tmQ, &sm->q_full, 0, qt[1] * kTile, bh);
+        tma_load_3d(sQ + kTileBytes + kBox, &tmQ, &sm->q_full, 64, qt[1] * kTile, bh);
+      }
     }
-    for (int j = 0; j < nkv; ++j) {
-      const int st = j % NST, round = j / NST;
+    for (int j = 0; j < nkv_max; ++j) {
+      const int st = j % kNst, round = j / kNst;
       if (round > 0) {
         bool ok = mbar_wait(&sm->kv_empty[st], (round - 1) & 1, abort);
         if (__any_sync(0xffffffffu, !ok)) break;
@@ -116,83 +135,93 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc_qk = idesc_bf16_f32(kTile, kTile, false, false);
     constexpr uint32_t idesc_pv = idesc_bf16_f32(kTile, kD, false, true);
-    const uint32_t q_addr = smem_u32(sQ);
-    auto issue_s = [&](int j) {
-      const int st = j % NST;
-      const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
-      const uint32_t d_tmem = tbase + ((j & 1) ? kColS1 : kColS0);
+    auto issue_s = [&](int x, int j) {
+      const uint32_t q_addr = smem_u32(sQ + x * kTileBytes);
+      const uint32_t k_addr = smem_u32(sK + (j % kNst) * kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < kD / 16; ++kk) {
         const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-        mma_ss(d_tmem, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk,
-               kk > 0);
+        mma_ss(tbase + col_s(x), smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
+               idesc_qk, kk > 0);
       }
-      mma_commit(&sm->s_full[j & 1]);
+      mma_commit(&sm->s_full[x]);
     };
-    bool ok = mbar_wait(&sm->q_full, 0, abort);
-    ok = ok && mbar_wait(&sm->k_full[0], 0, abort);
+    auto issue_pv = [&](int x, int j, int nkv_x) {
+      const uint32_t v_addr = smem_u32(sV + (j % kNst) * kTileBytes);
+#pragma unroll
+      for (int kk = 0; kk < kTile / 16; ++kk)
+        // 16 key rows per step: P columns advance by 8 (two bf16 per column),
+        // V rows advance by 16 x 128 B; the two 64-wide d blocks sit kBox apart.
+        mma_ts(tbase + col_o(x), tbase + col_s(x) + kk * 8, smem_desc_sw128(v_addr + kk * 2048, kBox, 1024),
+               idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+      if (j == nkv_x - 1) mma_commit(&sm->o_final[x]);
+    };
+    bool ok = mbar_wait(&sm->q_full, 0, abort) && mbar_wait(&sm->k_full[0], 0, abort);
     if (!__any_sync(0xffffffffu, !ok)) {
       tc_fence_after();
-      if (lane == 0) issue_s(0);
+      if (lane == 0) {
+        issue_s(0, 0);
+        if (nkv[1] > 0) issue_s(1, 0);
+      }
       __syncwarp();
-      for (int j = 0; j < nkv; ++j) {
-        if (j + 1 < nkv) {
-          ok = mbar_wait(&sm->k_full[(j + 1) % NST], ((j + 1) / NST) & 1, abort);
-          if (__any_sync(0xffffffffu, !ok)) break;
+      for (int j = 0; j < nkv_max && ok; ++j) {
+        const int st = j % kNst;
+        ok = mbar_wait(&sm->v_full[st], (j / kNst) & 1, abort);
+        if (__any_sync(0xffffffffu, !ok)) break;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const int nkv_x = x ? nkv[1] : nkv[0];
+          if (j >= nkv_x) continue;
+          ok = mbar_wait(&sm->p_ready[x], j & 1, abort);
+          if (j + 1 < nkv_x) ok = ok && mbar_wait(&sm->k_full[(j + 1) % kNst], ((j + 1) / kNst) & 1, abort);
+          if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
           tc_fence_after();
-          if (lane == 0) issue_s(j + 1);
+          if (lane == 0) {
+            issue_pv(x, j, nkv_x);
+            if (j + 1 < nkv_x) issue_s(x, j + 1);
+          }
           __syncwarp();
         }
-        const int st = j % NST;
-        ok = mbar_wait(&sm->v_full[st], (j / NST) & 1, abort);
-        ok = ok && mbar_wait(&sm->p_full[j & 1], (j >> 1) & 1, abort);
-        if (__any_sync(0xffffffffu, !ok)) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
-          const uint32_t p_tmem = tbase + ((j & 1) ? kColS1 : kColS0);
-#pragma unroll
-          for (int kk = 0; kk < kTile / 16; ++kk) {
-            // 16 key rows per step: P columns advance by 8 (two bf16 per column),
-            // V rows advance by 16 x 128 B; the two 64-wide d blocks sit kBox apart.
-            mma_ts(tbase + kColO, p_tmem + kk * 8, smem_desc_sw128(v_addr + kk * 2048, kBox, 1024), idesc_pv,
-                   (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          mma_commit(&sm->o_done);
-          mma_commit(&sm->kv_empty[st]);
-          if (j == nkv - 1) mma_commit(&sm->o_final);
-        }
+        if (!ok) break;
+        if (lane == 0) mma_commit(&sm->kv_empty[st]);
         __syncwarp();
       }
     }
+  }
   } else {
-    // ------------------------------------------------------------ softmax
+    // ------------------------------------------------------------ softmax (tile A: warps 4-7, B: 8-11)
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
+    const int x = warp < 8 ? 0 : 1;
+    const int my_qt = x ? qt[1] : qt[0];
+    const int my_nkv = x ? nkv[1] : nkv[0];
+    const int my_qlo = x ? q_lo[1] : q_lo[0];
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const int qrow = qt * kTile + row;          // row inside this (b,h) slice of Q
-    const int qpos = q_off + qrow;              // global causal position
+    const int qrow = my_qt * kTile + row;        // row inside this (b,h) slice of Q
+    const int qpos = q_off + qrow;               // global causal position
     const uint32_t lane_base = tbase + ((uint32_t)(quad * 32) << 16);
+    const uint32_t s_col = col_s(x), o_col = col_o(x);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      const int b = j & 1;
-      const uint32_t s_col = b ? kColS1 : kColS0;
-      ok = mbar_wait(&sm->s_full[b], (j >> 1) & 1, abort);
+    for (int j = 0; j < my_nkv; ++j) {
+      ok = mbar_wait(&sm->s_full[x], j & 1, abort);
       if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
       tc_fence_after();
       uint32_t s[4][32];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + s_col + c * 32, s[c]);
       tmem_ld_wait();
-      const bool need_mask = (j * kTile + kTile - 1 > q_lo) || (j * kTile + kTile > S_kv);
+      const bool need_mask = (j * kTile + kTile - 1 > my_qlo) || (j * kTile + kTile > S_kv);
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           float v = __uint_as_float(s[c][e]);
-          const int kvpos = j * kTile + c * 32 + e;
-          if (need_mask && (kvpos > qpos || kvpos >= S_kv)) { v = -INFINITY; s[c][e] = __float_as_uint(v); }
+          if (need_mask) {
+            const int kvpos = j * kTile + c * 32 + e;
+            if (kvpos > qpos || kvpos >= S_kv) { v = -INFINITY; s[c][e] = __float_as_uint(v); }
+          }
           mx = fmaxf(mx, v);
         }
       }
@@ -200,21 +229,18 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       if (j == 0) {
         m = mx2;
       } else if (__any_sync(0xffffffffu, mx2 > m + 8.0f)) {
+        // O_X already holds PV_X(j-1): S_X(j) was issued after it.
         const float mnew = fmaxf(m, mx2);
         const float alpha = ex2(m - mnew);
-        ok = mbar_wait(&sm->o_done, (j - 1) & 1, abort);
-        if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
-        tc_fence_after();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
-          tmem_ld32(lane_base + kColO + c * 32, o);
+          tmem_ld32(lane_base + o_col + c * 32, o);
           tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(lane_base + kColO + c * 32, o);
+          tmem_st32(lane_base + o_col + c * 32, o);
         }
-        tmem_st_wait();
         l *= alpha;
         m = mnew;
       }
@@ -235,17 +261,17 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       tmem_st_wait();
       l += rs;
       tc_fence_before();
-      mbar_arrive(&sm->p_full[b]);
+      mbar_arrive(&sm->p_ready[x]);
     }
-    if (ok) ok = mbar_wait(&sm->o_final, 0, abort);
-    if (!__any_sync(0xffffffffu, !ok)) {
+    if (ok && my_nkv > 0) ok = mbar_wait(&sm->o_final[x], 0, abort);
+    if (my_nkv > 0 && !__any_sync(0xffffffffu, !ok)) {
       tc_fence_after();
       const float inv_l = 1.0f / l;
       __nv_bfloat16* orow = O + ((size_t)bh * S_q + qrow) * kD;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
-        tmem_ld32(lane_base + kColO + c * 32, o);
+        tmem_ld32(lane_base + o_col + c * 32, o);
         tmem_ld_wait();
         if (qrow < S_q) {
 #pragma unroll
@@ -262,6 +288,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       if (qrow < S_q) LSE[(size_t)bh * S_q + qrow] = (m + __log2f(l)) * 0.69314718055994531f;
     }
   }
+
 
   tc_fence_before();
   __syncthreads();
@@ -304,19 +331,18 @@ int make_tmap_rows(CUtensorMap* m, const void* ptr, int rows, int BH) {
 
 int attn_fwd(const void* q, const void* k, const void* v, int B, int H, int S_q, int S_kv, int q_off, int D,
              float scale, void* o, float* lse, cudaStream_t st) {
-  constexpr int NST = 2;
   CUtensorMap mq, mk, mv;
   int rc;
   if ((rc = make_tmap_rows(&mq, q, S_q, B * H))) return rc;
   if ((rc = make_tmap_rows(&mk, k, S_kv, B * H))) return rc;
   if ((rc = make_tmap_rows(&mv, v, S_kv, B * H))) return rc;
   const int n_qt = (S_q + fwd::kTile - 1) / fwd::kTile;
-  const size_t smem = 1024 + fwd::kTileBytes * (1 + 2 * NST) + sizeof(FwdSmem<NST>);
-  auto kern = attn_fwd_kernel<NST>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dim3 grid(B * H, n_qt);
-  kern<<<grid, fwd::kThreads, smem, st>>>(mq, mk, mv, (__nv_bfloat16*)o, lse, S_q, S_kv, q_off, n_qt,
-                                           scale * 1.4426950408889634f);
+  const int n_pairs = (n_qt + 1) / 2;
+  const size_t smem = 1024 + fwd::kTileBytes * (2 + 2 * fwd::kNst) + sizeof(FwdSmem);
+  cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(B * H, n_pairs);
+  attn_fwd_kernel<<<grid, fwd::kThreads, smem, st>>>(mq, mk, mv, (__nv_bfloat16*)o, lse, S_q, S_kv, q_off, n_pairs,
+                                                    scale * 1.4426950408889634f);
   return check_launch("attn_fwd_kernel");
 }
 

@@ -34,8 +34,8 @@ constexpr int kSelTopk = 128;
 constexpr int kSelHalf = 64;
 constexpr float kNegBig = -1e6f;   // placeholder score (reference :191-194, :227)
 
-// One comparator stage (k, j) of the descending bitonic network.
-// NP = number of payload arrays moved with the key.
+// One comparator stage (k, j) of the descending bitonic network, branch-free.
+// NP = number of payload arrays moved with the key (1: index; 2: index + score).
 template <int NP>
 __device__ __forceinline__ void bitonic_stage(int k, int j, int lane, float (&key)[4], float (&pf)[4],
                                               int (&ix)[4]) {
@@ -47,11 +47,17 @@ __device__ __forceinline__ void bitonic_stage(int k, int j, int lane, float (&ke
       const int hi = lo | rr;
       const int i_lo = lane + 32 * lo;
       const bool desc = (i_lo & k) == 0;
-      const bool swap = desc ? (key[lo] < key[hi]) : (key[lo] > key[hi]);
-      if (swap) {
-        float t = key[lo]; key[lo] = key[hi]; key[hi] = t;
-        int ti = ix[lo]; ix[lo] = ix[hi]; ix[hi] = ti;
-        if (NP > 1) { float tp = pf[lo]; pf[lo] = pf[hi]; pf[hi] = tp; }
+      const float a = key[lo], b = key[hi];
+      const bool swap = desc ? (a < b) : (a > b);
+      key[lo] = swap ? b : a;
+      key[hi] = swap ? a : b;
+      const int ia = ix[lo], ib = ix[hi];
+      ix[lo] = swap ? ib : ia;
+      ix[hi] = swap ? ia : ib;
+      if (NP > 1) {
+        const float pa = pf[lo], pb = pf[hi];
+        pf[lo] = swap ? pb : pa;
+        pf[hi] = swap ? pa : pb;
       }
     }
   } else {
@@ -64,41 +70,65 @@ __device__ __forceinline__ void bitonic_stage(int k, int j, int lane, float (&ke
       const int oi = __shfl_xor_sync(0xffffffffu, ix[r], j);
       float op = 0.f;
       if (NP > 1) op = __shfl_xor_sync(0xffffffffu, pf[r], j);
-      const bool swap = lower ? (desc ? (key[r] < o) : (key[r] > o)) : (desc ? (key[r] > o) : (key[r] < o));
-      if (swap) { key[r] = o; ix[r] = oi; if (NP > 1) pf[r] = op; }
+      // lower partner keeps the larger value when descending; strict compares keep ties in place
+      const bool swap = (lower == desc) ? (key[r] < o) : (key[r] > o);
+      key[r] = swap ? o : key[r];
+      ix[r] = swap ? oi : ix[r];
+      if (NP > 1) pf[r] = swap ? op : pf[r];
     }
   }
 }
 
+struct SortSet2 { float key[4]; float pf[4]; int ix[4]; };   // qk sort: key qk, payload kq score + index
+struct SortSet1 { float key[4]; float pf[4]; int ix[4]; };   // kq sort: key kq, payload index
+
 // The (k, j) stage sequence is expanded at compile time so that every
-// register index and direction test in bitonic_stage is a constant.
-template <int NP, int K, int J>
+// register index and direction test in bitonic_stage is a constant.  The
+// dual form runs two independent networks stage by stage for twice the
+// instruction-level parallelism of a single warp.
+template <int K, int J, bool DUAL>
 struct BitonicStages {
-  static __device__ __forceinline__ void run(int lane, float (&key)[4], float (&pf)[4], int (&ix)[4]) {
-    bitonic_stage<NP>(K, J, lane, key, pf, ix);
-    BitonicStages<NP, K, J / 2>::run(lane, key, pf, ix);
+  static __device__ __forceinline__ void run(int lane, SortSet2& a, SortSet1& b) {
+    if (DUAL) bitonic_stage<2>(K, J, lane, a.key, a.pf, a.ix);
+    bitonic_stage<1>(K, J, lane, b.key, b.pf, b.ix);
+    BitonicStages<K, J / 2, DUAL>::run(lane, a, b);
   }
 };
-template <int NP, int K>
-struct BitonicStages<NP, K, 0> {
-  static __device__ __forceinline__ void run(int, float (&)[4], float (&)[4], int (&)[4]) {}
+template <int K, bool DUAL>
+struct BitonicStages<K, 0, DUAL> {
+  static __device__ __forceinline__ void run(int, SortSet2&, SortSet1&) {}
 };
-template <int NP, int K>
+template <int K, bool DUAL>
 struct BitonicNet {
-  static __device__ __forceinline__ void run(int lane, float (&key)[4], float (&pf)[4], int (&ix)[4]) {
-    BitonicNet<NP, K / 2>::run(lane, key, pf, ix);
-    BitonicStages<NP, K, K / 2>::run(lane, key, pf, ix);
+  static __device__ __forceinline__ void run(int lane, SortSet2& a, SortSet1& b) {
+    BitonicNet<K / 2, DUAL>::run(lane, a, b);
+    BitonicStages<K, K / 2, DUAL>::run(lane, a, b);
   }
 };
-template <int NP>
-struct BitonicNet<NP, 1> {
-  static __device__ __forceinline__ void run(int, float (&)[4], float (&)[4], int (&)[4]) {}
+template <bool DUAL>
+struct BitonicNet<1, DUAL> {
+  static __device__ __forceinline__ void run(int, SortSet2&, SortSet1&) {}
 };
 
-template <int NP>
-__device__ __forceinline__ void bitonic128(int lane, float (&key)[4], float (&pf)[4], int (&ix)[4]) {
-  BitonicNet<NP, kSelTopk>::run(lane, key, pf, ix);
-}
+// qk network on a alone (the kq set is untouched): stages on a only.
+template <int K, int J>
+struct QkStages {
+  static __device__ __forceinline__ void run(int lane, SortSet2& a) {
+    bitonic_stage<2>(K, J, lane, a.key, a.pf, a.ix);
+    QkStages<K, J / 2>::run(lane, a);
+  }
+};
+template <int K>
+struct QkStages<K, 0> { static __device__ __forceinline__ void run(int, SortSet2&) {} };
+template <int K>
+struct QkNet {
+  static __device__ __forceinline__ void run(int lane, SortSet2& a) {
+    QkNet<K / 2>::run(lane, a);
+    QkStages<K, K / 2>::run(lane, a);
+  }
+};
+template <>
+struct QkNet<1> { static __device__ __forceinline__ void run(int, SortSet2&) {} };
 
 struct SelGeom {
   int N, L, p, shift, T, ncc, S_tot, S_sel, chunk_len;
@@ -149,44 +179,49 @@ select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ s
     };
     auto valid = [&](int kidx) { return kidx >= 0 && kidx <= K_end; };
 
-    // qk arrays (regs 0,1 = running top-64 by qk; regs 2,3 = new batch)
-    float qs[4], ks[4];
-    int ix[4];
-    // kq top-64 (regs 0,1 of the kq sort)
-    float tks[2];
-    int tki[2];
+    // qk set: regs 0,1 = running top-64 by qk, regs 2,3 = the batch being sorted.
+    // kq set: regs 0,1 = running top-64 by kq, regs 2,3 = the qk rejects.
+    SortSet2 qk;
+    SortSet1 kq;
 #pragma unroll
-    for (int r = 0; r < 2; ++r) { qs[r] = kNegBig; ks[r] = kNegBig; ix[r] = -1; tks[r] = kNegBig; tki[r] = -1; }
+    for (int r = 0; r < 4; ++r) { qk.key[r] = kNegBig; qk.pf[r] = kNegBig; qk.ix[r] = -1; kq.key[r] = kNegBig; kq.pf[r] = 0.f; kq.ix[r] = -1; }
 
     const int nb = (ncand + kSelHalf - 1) / kSelHalf;
     int nidx[2];
     float nq[2], nk[2];
+    auto fetch = [&](int bt) {
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      nidx[r] = cand(lane + 32 * r);
-      nq[r] = valid(nidx[r]) ? __ldg(sq + lvl_off + nidx[r]) : kNegBig;
-      nk[r] = valid(nidx[r]) ? __ldg(sk + lvl_off + nidx[r]) : kNegBig;
-    }
-    for (int bt = 0; bt < nb; ++bt) {
-#pragma unroll
-      for (int r = 0; r < 2; ++r) { ix[2 + r] = nidx[r]; qs[2 + r] = nq[r]; ks[2 + r] = nk[r]; }
-      if (bt + 1 < nb) {
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          nidx[r] = cand((bt + 1) * kSelHalf + lane + 32 * r);
-          nq[r] = valid(nidx[r]) ? __ldg(sq + lvl_off + nidx[r]) : kNegBig;
-          nk[r] = valid(nidx[r]) ? __ldg(sk + lvl_off + nidx[r]) : kNegBig;
-        }
+      for (int r = 0; r < 2; ++r) {
+        nidx[r] = cand(bt * kSelHalf + lane + 32 * r);
+        nq[r] = valid(nidx[r]) ? __ldg(sq + lvl_off + nidx[r]) : kNegBig;
+        nk[r] = valid(nidx[r]) ? __ldg(sk + lvl_off + nidx[r]) : kNegBig;
       }
-      // qk sort of [top-64 by qk ; batch]          (reference :203-232)
-      bitonic128<2>(lane, qs, ks, ix);
-      // kq sort of [top-64 by kq ; qk rejects]     (reference :242-253)
-      float kk[4] = {tks[0], tks[1], ks[2], ks[3]};
-      int ki[4] = {tki[0], tki[1], ix[2], ix[3]};
-      float dummy[4];
-      bitonic128<1>(lane, kk, dummy, ki);
-      tks[0] = kk[0]; tks[1] = kk[1]; tki[0] = ki[0]; tki[1] = ki[1];
+    };
+    auto take = [&]() {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) { qk.ix[2 + r] = nidx[r]; qk.key[2 + r] = nq[r]; qk.pf[2 + r] = nk[r]; }
+    };
+    fetch(0);
+    take();
+    if (nb > 1) fetch(1);
+    // qk sort of batch 0 (reference :203-232)
+    QkNet<kSelTopk>::run(lane, qk);
+    for (int bt = 0; bt < nb; ++bt) {
+      // kq set for batch bt: its top-64 and the qk rejects (reference :242-250)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) { kq.key[2 + r] = qk.pf[2 + r]; kq.ix[2 + r] = qk.ix[2 + r]; }
+      if (bt + 1 < nb) {
+        take();                                  // batch bt+1 joins the qk top-64
+        if (bt + 2 < nb) fetch(bt + 2);
+        // kq sort of batch bt and qk sort of batch bt+1 are independent: run them together
+        BitonicNet<kSelTopk, true>::run(lane, qk, kq);
+      } else {
+        BitonicNet<kSelTopk, false>::run(lane, qk, kq);
+      }
     }
+    int tki[2], ix[2];
+    tki[0] = kq.ix[0]; tki[1] = kq.ix[1];
+    ix[0] = qk.ix[0]; ix[1] = qk.ix[1];
     __syncwarp();
     // Parents of the next level: [top-64 by qk ; top-64 by kq] (reference :324-327)
     s_parent[lane] = ix[0];

@@ -16,8 +16,8 @@
 //               dV_j += P^T dO_i             (TS, TMEM cols 256..383)
 //               dK_j += dS^T Q_i             (SS, TMEM cols 384..511)
 //               dQ_i  = dS K_j               (SS, dS read MN-major; TMEM cols 128..255)
-//             the softmax warps then drain dQ_i from TMEM into the fp32 dQacc
-//             with vector atomics.  Eight compute warps: two per TMEM lane
+//             the softmax warps then move dQ_i from TMEM into a swizzled fp32
+//             shared-memory stage that a TMA reduce-add adds into dQacc.  Eight compute warps: two per TMEM lane
 //             quadrant, each owning 64 of the 128 columns.  At the end dK (times scale) and dV are
 //             written as bf16.
 //   3. post:  dQ = bf16(dQacc * scale)
@@ -36,6 +36,7 @@ using namespace sm100;
 
 __device__ int g_attn_bwd_status;   // set to 1 when a bounded wait gave up
 int make_tmap_rows(CUtensorMap* m, const void* ptr, int rows, int BH);
+int make_tmap_rows_f32(CUtensorMap* m, const void* ptr, int rows, int BH);
 
 namespace bwd {
 constexpr int kTile = 128;
@@ -44,6 +45,7 @@ constexpr int kBox = 16384;
 constexpr int kTileBytes = 2 * kBox;
 constexpr int kThreads = 320;   // producer, MMA, 8 compute warps (2 per TMEM lane quadrant)
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384, kTmemCols = 512;
+constexpr int kDqStageBytes = 4 * kBox;   // 128 x 128 fp32
 }  // namespace bwd
 
 struct BwdSmem {
@@ -71,18 +73,22 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int r, int c, uint4 v) {
 __global__ void __launch_bounds__(bwd::kThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                const float* __restrict__ LSE, const float* __restrict__ Delta, float* __restrict__ dQacc,
+                const __grid_constant__ CUtensorMap tmdQ,
+                const float* __restrict__ LSE, const float* __restrict__ Delta,
                 __nv_bfloat16* __restrict__ dK, __nv_bfloat16* __restrict__ dV, int S_q, int S_kv, int q_off,
                 float scale2, float scale) {
   using namespace bwd;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 5 bf16 tiles + the fp32 dQ stage + barriers fill 227 KB: no room for
+  // alignment slack, so the dynamic window itself must be 1024-byte aligned.
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = smem_raw;
   uint8_t* sK = base;
   uint8_t* sV = base + kTileBytes;
   uint8_t* sQ = base + 2 * kTileBytes;
   uint8_t* sdO = base + 3 * kTileBytes;
   uint8_t* sdS = base + 4 * kTileBytes;
-  BwdSmem* sm = reinterpret_cast<BwdSmem*>(base + 5 * kTileBytes);
+  uint8_t* sdQ = base + 5 * kTileBytes;          // fp32 dQ_i stage: 4 boxes of 128 rows x 32 floats, SW128
+  BwdSmem* sm = reinterpret_cast<BwdSmem*>(base + 5 * kTileBytes + kDqStageBytes);
 
   const int bh = blockIdx.x;
   const int j = blockIdx.y;                      // key tile (heaviest first: j = 0 sees every query)
@@ -92,6 +98,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const int n_it = n_qt - i0 > 0 ? n_qt - i0 : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (*reinterpret_cast<volatile int*>(&g_attn_bwd_status)) return;
+  if (smem_u32(smem_raw) & 1023u) {               // layout assumption broken: report instead of corrupting
+    if (threadIdx.x == 0) atomicExch(&g_attn_bwd_status, 1);
+    return;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(&sm->kv_full, 1);
@@ -145,16 +155,23 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     bool ok = n_it > 0 ? mbar_wait(&sm->kv_full, 0, abort) : true;
     for (int t = 0; t < n_it; ++t) {
       ok = ok && mbar_wait(&sm->q_full, t & 1, abort);
-      if (t > 0) ok = ok && mbar_wait(&sm->dq_free, (t - 1) & 1, abort);
       if (__any_sync(0xffffffffu, !ok)) break;
       tc_fence_after();
       if (lane == 0) {
+        // S^T: the S columns are free (P_{i-1} was read by the dV MMA already issued)
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
           mma_ss(tbase + kColS, smem_desc_sw128(aK + off, 16, 1024), smem_desc_sw128(aQ + off, 16, 1024), id_kk,
                  kk > 0);
         }
+      }
+      __syncwarp();
+      // dP^T reuses the columns of dQ_{i-1}: wait until the compute warps have read it
+      if (t > 0) ok = mbar_wait(&sm->dq_free, (t - 1) & 1, abort);
+      if (__any_sync(0xffffffffu, !ok)) break;
+      tc_fence_after();
+      if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
@@ -222,21 +239,27 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           tmem_ld_wait();
           uint32_t dsw[16];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float pr[2], dr[2];
+          for (int e = 0; e < 32; e += 4) {
+            const float4 L4 = *reinterpret_cast<const float4*>(&sm->lse2[buf][c * 32 + e]);
+            const float4 D4 = *reinterpret_cast<const float4*>(&sm->delta[buf][c * 32 + e]);
+            const float Ls[4] = {L4.x, L4.y, L4.z, L4.w};
+            const float Ds[4] = {D4.x, D4.y, D4.z, D4.w};
+            float pr[4], dr[4];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
+            for (int u = 0; u < 4; ++u) {
               const int ql = c * 32 + e + u;
-              float p = ex2(fmaf(__uint_as_float(s[e + u]), scale2, -sm->lse2[buf][ql]));
+              float p = ex2(fmaf(__uint_as_float(s[e + u]), scale2, -Ls[u]));
               if (need_mask) {
                 const int qpos = q_lo + ql;
                 if (kv_pos > qpos || i * kTile + ql >= S_q || kv_pos >= S_kv) p = 0.f;
               }
               pr[u] = p;
-              dr[u] = p * (__uint_as_float(dp[e + u]) - sm->delta[buf][ql]);
+              dr[u] = p * (__uint_as_float(dp[e + u]) - Ds[u]);
             }
             pk[c2 * 16 + e / 2] = pack_bf16(pr[0], pr[1]);
+            pk[c2 * 16 + e / 2 + 1] = pack_bf16(pr[2], pr[3]);
             dsw[e / 2] = pack_bf16(dr[0], dr[1]);
+            dsw[e / 2 + 1] = pack_bf16(dr[2], dr[3]);
           }
 #pragma unroll
           for (int v = 0; v < 4; ++v)
@@ -252,25 +275,31 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       ok = mbar_wait(&sm->dq_ready, t & 1, abort);
       if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
       tc_fence_after();
-      const int qrow = i * kTile + r;
-      float* dst = dQacc + ((size_t)bh * S_q + qrow) * kD;
+      // dQ_i (TMEM lane = query row) -> swizzled fp32 stage -> TMA reduce-add into dQacc
+      if (tid == 0 && t > 0) bulk_wait_read_all();  // previous reduce has read the stage
+      named_bar_sync(1, 256);
 #pragma unroll
       for (int c2 = 0; c2 < 2; ++c2) {
-        const int c = 2 * g + c2;                   // this warp's 64 d columns
+        const int c = 2 * g + c2;                   // this warp's 32-column chunk = stage box c
         uint32_t v[32];
         tmem_ld32(lane_base + kColDP + c * 32, v);
         tmem_ld_wait();
-        if (qrow < S_q) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + e),
-                      make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]), __uint_as_float(v[e + 2]),
-                                  __uint_as_float(v[e + 3])));
-        }
+        for (int ch = 0; ch < 8; ++ch)
+          *reinterpret_cast<uint4*>(sdQ + c * kBox + r * 128 + ((ch ^ (r & 7)) << 4)) =
+              make_uint4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
       }
       tc_fence_before();
       mbar_arrive(&sm->dq_free);
+      fence_async_smem();
+      named_bar_sync(1, 256);
+      if (tid == 0) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) tma_reduce_add_3d(&tmdQ, sdQ + b * kBox, 32 * b, i * kTile, bh);
+        bulk_commit();
+      }
     }
+    if (tid == 0) bulk_wait_all();
     // epilogue: dV and dK rows of this key tile
     if (!__any_sync(0xffffffffu, !ok)) {
       tc_fence_after();
@@ -377,16 +406,18 @@ int attn_bwd(const void* q, const void* k, const void* v, const void* o, const f
   if ((rc = make_tmap_rows(&mk, k, S_kv, B * H))) return rc;
   if ((rc = make_tmap_rows(&mv, v, S_kv, B * H))) return rc;
   if ((rc = make_tmap_rows(&mdo, dO, S_q, B * H))) return rc;
+  CUtensorMap mdq;
+  if ((rc = make_tmap_rows_f32(&mdq, dQacc, S_q, B * H))) return rc;
   {
     const long long threads = (long long)rows * 32;
     attn_bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
         (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, Delta, dQacc, (long long)rows);
     if ((rc = check_launch("attn_bwd_prep_kernel"))) return rc;
   }
-  const size_t smem = 1024 + 5 * bwd::kTileBytes + sizeof(BwdSmem);
+  const size_t smem = 5 * bwd::kTileBytes + bwd::kDqStageBytes + sizeof(BwdSmem);
   cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid(B * H, (S_kv + bwd::kTile - 1) / bwd::kTile);
-  attn_bwd_kernel<<<grid, bwd::kThreads, smem, st>>>(mq, mk, mv, mdo, lse, Delta, dQacc, (__nv_bfloat16*)dk,
+  attn_bwd_kernel<<<grid, bwd::kThreads, smem, st>>>(mq, mk, mv, mdo, mdq, lse, Delta, (__nv_bfloat16*)dk,
                                                     (__nv_bfloat16*)dv, S_q, S_kv, q_off,
                                                     scale * 1.4426950408889634f, scale);
   if ((rc = check_launch("attn_bwd_kernel"))) return rc;

@@ -329,6 +329,23 @@ int make_tmap_rows(CUtensorMap* m, const void* ptr, int rows, int BH) {
   return LH_OK;
 }
 
+// (BH, rows, 128) fp32 tensor viewed as 3-D {128, rows, BH}; boxes of 32
+// columns (128 bytes) x 128 rows with the 128-byte swizzle (dQ accumulator).
+int make_tmap_rows_f32(CUtensorMap* m, const void* ptr, int rows, int BH) {
+  auto enc = get_encode_fn();
+  if (!enc) { set_error("cuTensorMapEncodeTiled unavailable"); return LH_ERR_LAUNCH; }
+  if ((uintptr_t)ptr & 15) { set_error("dQ accumulator must be 16-byte aligned"); return LH_ERR_ARG; }
+  cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {128 * 4, (cuuint64_t)rows * 128 * 4};
+  cuuint32_t box[3] = {32, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled (f32) failed (%d)", (int)r); return LH_ERR_LAUNCH; }
+  return LH_OK;
+}
+
 int attn_fwd(const void* q, const void* k, const void* v, int B, int H, int S_q, int S_kv, int q_off, int D,
              float scale, void* o, float* lse, cudaStream_t st) {
   CUtensorMap mq, mk, mv;

@@ -43,7 +43,7 @@ constexpr int kTile = 128;
 constexpr int kD = 128;
 constexpr int kBox = 16384;
 constexpr int kTileBytes = 2 * kBox;
-constexpr int kThreads = 320;   // producer, MMA, 8 compute warps (2 per TMEM lane quadrant)
+constexpr int kThreads = 384;   // {producer, MMA, 2 idle}, then 8 compute warps (2 per TMEM lane quadrant)
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384, kTmemCols = 512;
 constexpr int kDqStageBytes = 4 * kBox;   // 128 x 128 fp32
 }  // namespace bwd
@@ -121,6 +121,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tbase = sm->tmem_base;
   volatile int* abort = &sm->abort;
 
+  if (warp < 4) {
+  // Warpgroup 0 hands registers to the compute warpgroups: 96 + 2 x 200 per
+  // thread-slot stays within the 3 x 168 of the launch (one aligned setmaxnreg per warpgroup).
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 96;\n" ::: "memory");
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && n_it > 0) {
@@ -204,11 +208,13 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       }
       __syncwarp();
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
     // ------------------------------------------------------------ softmax / dS / drain
     const int quad = warp & 3;
     const int r = quad * 32 + lane;                 // key row inside the tile (TMEM lane)
-    const int tid = threadIdx.x - 64;               // 0..255
+    const int tid = threadIdx.x - 128;              // 0..255
     const int g = tid >> 7;                         // column half: query columns / d columns [64g, 64g+64)
     const int kv_pos = j * kTile + r;
     const uint32_t lane_base = tbase + ((uint32_t)(quad * 32) << 16);
@@ -230,13 +236,19 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       {
         const int h = g;                            // this warp's 64 query columns
         uint32_t pk[32];
+        // both 32-column chunks of S and dP in flight before a single wait
+        uint32_t s2[2][32], dp2[2][32];
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          tmem_ld32(lane_base + kColS + (h * 2 + c2) * 32, s2[c2]);
+          tmem_ld32(lane_base + kColDP + (h * 2 + c2) * 32, dp2[c2]);
+        }
+        tmem_ld_wait();
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2) {
           const int c = h * 2 + c2;                 // 32-column chunk
-          uint32_t s[32], dp[32];
-          tmem_ld32(lane_base + kColS + c * 32, s);
-          tmem_ld32(lane_base + kColDP + c * 32, dp);
-          tmem_ld_wait();
+          const uint32_t (&s)[32] = s2[c2];
+          const uint32_t (&dp)[32] = dp2[c2];
           uint32_t dsw[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {

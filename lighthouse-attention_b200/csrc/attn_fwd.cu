@@ -212,7 +212,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + s_col + c * 32, s[c]);
       tmem_ld_wait();
       const bool need_mask = (j * kTile + kTile - 1 > my_qlo) || (j * kTile + kTile > S_kv);
-      float mx = -INFINITY;
+      // eight independent partial maxima instead of one 128-long dependency chain
+      float mxp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
 #pragma unroll
@@ -222,9 +225,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             const int kvpos = j * kTile + c * 32 + e;
             if (kvpos > qpos || kvpos >= S_kv) { v = -INFINITY; s[c][e] = __float_as_uint(v); }
           }
-          mx = fmaxf(mx, v);
+          mxp[e & 7] = fmaxf(mxp[e & 7], v);
         }
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       const float mx2 = mx * scale2;
       if (j == 0) {
         m = mx2;
@@ -244,7 +249,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         l *= alpha;
         m = mnew;
       }
-      float rs = 0.f;
+      float rsp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) rsp[u] = 0.f;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t pk[32];
@@ -253,11 +260,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           const int i0 = h * 64 + 2 * e;
           const float p0 = ex2(fmaf(__uint_as_float(s[i0 >> 5][i0 & 31]), scale2, -m));
           const float p1 = ex2(fmaf(__uint_as_float(s[(i0 + 1) >> 5][(i0 + 1) & 31]), scale2, -m));
-          rs += p0 + p1;
+          rsp[e & 7] += p0 + p1;
           pk[e] = pack_bf16(p0, p1);
         }
         tmem_st32(lane_base + s_col + h * 32, pk);
       }
+      const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       tmem_st_wait();
       l += rs;
       tc_fence_before();

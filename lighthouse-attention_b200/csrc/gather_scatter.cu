@@ -2,6 +2,8 @@
 // deterministic fan-out scatter (forward + adjoint), the inverse map, and the
 // un-pool backward.  All are HBM-bound row copies with 16-byte accesses; each
 // thread owns one 16-byte chunk of a D-wide row.
+#include <type_traits>
+
 #include "lh_common.cuh"
 
 namespace lh {
@@ -44,7 +46,7 @@ gather_kernel(const T* __restrict__ raw0, const T* __restrict__ raw1, const T* _
 // ---------------------------------------------------------------- scatter (pull)
 // out[bh, t] = sum_l attn[bh, inv(l, (t+1)/p^l - 1)] over levels whose item
 // window [j*f + f - 1, j*f + 2f - 1) contains t (reference :408-459).
-template <class T>
+template <class T, int LV>
 __global__ void __launch_bounds__(kRowThreads)
 scatter_fwd_kernel(const T* __restrict__ attn, const int32_t* __restrict__ inverse, Pyramid pyr, int p_shift,
                    int D, int S_sel, FastDiv fd_n, T* __restrict__ out, int cpr_shift, uint32_t n_chunks) {
@@ -58,19 +60,26 @@ scatter_fwd_kernel(const T* __restrict__ attn, const int32_t* __restrict__ inver
     float acc[VEC];
 #pragma unroll
     for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
+    // all index loads first, then all row loads: no dependent chains between levels
+    int slot[LV];
 #pragma unroll
-    for (int l = 0; l < 8; ++l) {
-      if (l >= pyr.L) break;
-      const int j = (int)((t + 1) >> (l * p_shift)) - 1;
-      if (j >= 0 && j < pyr.len[l]) {
-        const int slot = __ldg(inv + pyr.off[l] + j);
-        if (slot >= 0) {
-          float v[VEC];
-          load16(attn + ((size_t)bh * S_sel + slot) * D + c, v);
+    for (int l = 0; l < LV; ++l) {
+      const int jj = (int)((t + 1) >> (l * p_shift)) - 1;
+      slot[l] = (jj >= 0 && jj < pyr.len[l]) ? __ldg(inv + pyr.off[l] + jj) : -1;
+    }
+    float v[LV][VEC];
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) acc[e] += v[e];
-        }
+    for (int l = 0; l < LV; ++l) {
+      if (slot[l] >= 0) load16(attn + ((size_t)bh * S_sel + slot[l]) * D + c, v[l]);
+      else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) v[l][e] = 0.f;
       }
+    }
+#pragma unroll
+    for (int l = 0; l < LV; ++l) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] += v[l][e];
     }
     store16(out + (size_t)row * D + c, acc);
   }
@@ -127,7 +136,7 @@ __global__ void inverse_kernel(const int32_t* __restrict__ indices, int S_sel, i
 
 // ---------------------------------------------------------------- un-pool backward
 // dx[b, t, h] = sum_l dsel[bh, inv(off_l + t/p^l)] / p^l   (autograd of :800-813, :604-606)
-template <class T>
+template <class T, int LV>
 __global__ void __launch_bounds__(kRowThreads)
 unpool_bwd_kernel(const T* __restrict__ d0, const T* __restrict__ d1, const T* __restrict__ d2,
                   T* __restrict__ o0, T* __restrict__ o1, T* __restrict__ o2,
@@ -149,20 +158,26 @@ unpool_bwd_kernel(const T* __restrict__ d0, const T* __restrict__ d1, const T* _
     float acc[VEC];
 #pragma unroll
     for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
+    int slot[LV];
 #pragma unroll
-    for (int l = 0; l < 8; ++l) {
-      if (l >= pyr.L) break;
-      const int j = (int)(t >> (l * p_shift));
-      if (j < pyr.len[l]) {
-        const int slot = __ldg(inv + pyr.off[l] + j);
-        if (slot >= 0) {
-          float v[VEC];
-          load16(dsel + ((size_t)bh * S_sel + slot) * D + c, v);
-          const float sc = 1.0f / (float)(1 << (l * p_shift));
+    for (int l = 0; l < LV; ++l) {
+      const int jj = (int)(t >> (l * p_shift));
+      slot[l] = jj < pyr.len[l] ? __ldg(inv + pyr.off[l] + jj) : -1;
+    }
+    float v[LV][VEC];
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) acc[e] = fmaf(v[e], sc, acc[e]);
-        }
+    for (int l = 0; l < LV; ++l) {
+      if (slot[l] >= 0) load16(dsel + ((size_t)bh * S_sel + slot[l]) * D + c, v[l]);
+      else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) v[l][e] = 0.f;
       }
+    }
+#pragma unroll
+    for (int l = 0; l < LV; ++l) {
+      const float sc = 1.0f / (float)(1 << (l * p_shift));
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] = fmaf(v[l][e], sc, acc[e]);
     }
     store16(dx + (size_t)row * D + c, acc);
   }
@@ -175,6 +190,21 @@ static int grid_for(long long n) {
 }
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+// Calls f(std::integral_constant<int, L>) for L in [1, 7]; false otherwise.
+template <class F>
+static bool dispatch_levels(int L, F&& f) {
+  switch (L) {
+    case 1: f(std::integral_constant<int, 1>{}); return true;
+    case 2: f(std::integral_constant<int, 2>{}); return true;
+    case 3: f(std::integral_constant<int, 3>{}); return true;
+    case 4: f(std::integral_constant<int, 4>{}); return true;
+    case 5: f(std::integral_constant<int, 5>{}); return true;
+    case 6: f(std::integral_constant<int, 6>{}); return true;
+    case 7: f(std::integral_constant<int, 7>{}); return true;
+  }
+  return false;
+}
 
 static int log2i(int x) { int s = 0; while ((1 << s) < x) ++s; return s; }
 
@@ -220,10 +250,14 @@ int scatter_fwd(const void* attn, const int32_t* inverse, int dtype, int B, int 
   int rc = row_geometry("scatter_fwd", dtype, D, (long long)B * H * N_total, &cs, &n);
   if (rc) return rc;
   FastDiv fn(N_total);
-  if (dtype == LH_DTYPE_BF16)
-    scatter_fwd_kernel<__nv_bfloat16><<<grid_for(n), kRowThreads, 0, st>>>((const __nv_bfloat16*)attn, inverse, pyr, log2i(p), D, S_sel, fn, (__nv_bfloat16*)out, cs, n);
-  else
-    scatter_fwd_kernel<float><<<grid_for(n), kRowThreads, 0, st>>>((const float*)attn, inverse, pyr, log2i(p), D, S_sel, fn, (float*)out, cs, n);
+  auto go = [&](auto lv) {
+    constexpr int LV = decltype(lv)::value;
+    if (dtype == LH_DTYPE_BF16)
+      scatter_fwd_kernel<__nv_bfloat16, LV><<<grid_for(n), kRowThreads, 0, st>>>((const __nv_bfloat16*)attn, inverse, pyr, log2i(p), D, S_sel, fn, (__nv_bfloat16*)out, cs, n);
+    else
+      scatter_fwd_kernel<float, LV><<<grid_for(n), kRowThreads, 0, st>>>((const float*)attn, inverse, pyr, log2i(p), D, S_sel, fn, (float*)out, cs, n);
+  };
+  if (!dispatch_levels(L, go)) { set_error("scatter_fwd: L must be in [1, 7]"); return LH_ERR_SHAPE; }
   return check_launch("scatter_fwd_kernel");
 }
 
@@ -260,13 +294,17 @@ int unpool_bwd(const void* dq, const void* dk, const void* dv, const int32_t* in
   if (rc) return rc;
   dim3 grid(grid_for(n), 3);
   FastDiv fh(H), fs(S);
-  if (dtype == LH_DTYPE_BF16) {
-    using T = __nv_bfloat16;
-    unpool_bwd_kernel<T><<<grid, kRowThreads, 0, st>>>((const T*)dq, (const T*)dk, (const T*)dv, (T*)dxq, (T*)dxk, (T*)dxv, inverse, pyr, log2i(p), fh, fs, D, S_sel, cs, n);
-  } else {
-    using T = float;
-    unpool_bwd_kernel<T><<<grid, kRowThreads, 0, st>>>((const T*)dq, (const T*)dk, (const T*)dv, (T*)dxq, (T*)dxk, (T*)dxv, inverse, pyr, log2i(p), fh, fs, D, S_sel, cs, n);
-  }
+  auto go = [&](auto lv) {
+    constexpr int LV = decltype(lv)::value;
+    if (dtype == LH_DTYPE_BF16) {
+      using T = __nv_bfloat16;
+      unpool_bwd_kernel<T, LV><<<grid, kRowThreads, 0, st>>>((const T*)dq, (const T*)dk, (const T*)dv, (T*)dxq, (T*)dxk, (T*)dxv, inverse, pyr, log2i(p), fh, fs, D, S_sel, cs, n);
+    } else {
+      using T = float;
+      unpool_bwd_kernel<T, LV><<<grid, kRowThreads, 0, st>>>((const T*)dq, (const T*)dk, (const T*)dv, (T*)dxq, (T*)dxk, (T*)dxv, inverse, pyr, log2i(p), fh, fs, D, S_sel, cs, n);
+    }
+  };
+  if (!dispatch_levels(L, go)) { set_error("unpool_bwd: L must be in [1, 7]"); return LH_ERR_SHAPE; }
   return check_launch("unpool_bwd_kernel");
 }
 

@@ -75,18 +75,28 @@ pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T
       }
     };
     auto process = [&](int slot, int i0) {
+      // the U tokens' norm reductions run side by side (independent shuffle chains)
+      float nrms[U];
+      if (scored) {
+        float ss[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          ss[u] = 0.f;
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) ss[u] = fmaf(buf[slot][u][e], buf[slot][u][e], ss[u]);
+        }
+#pragma unroll
+        for (int m = LPH / 2; m > 0; m >>= 1) {
+#pragma unroll
+          for (int u = 0; u < U; ++u) ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], m, LPH);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) nrms[u] = round_to(sqrtf(ss[u]), (const T*)nullptr);
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int i = i0 + u;
-        float nrm = 0.f;
-        if (scored) {
-          float ss = 0.f;
-#pragma unroll
-          for (int e = 0; e < VEC; ++e) ss = fmaf(buf[slot][u][e], buf[slot][u][e], ss);
-#pragma unroll
-          for (int m = LPH / 2; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m, LPH);
-          nrm = round_to(sqrtf(ss), (const T*)nullptr);
-        }
+        const float nrm = scored ? nrms[u] : 0.f;
         if (i >= ntok || !active) continue;
         if (scored && c == 0) s_scores[h * tpc_tot + i] = nrm;
 #pragma unroll

@@ -257,16 +257,24 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             const float Ls[4] = {L4.x, L4.y, L4.z, L4.w};
             const float Ds[4] = {D4.x, D4.y, D4.z, D4.w};
             float pr[4], dr[4];
+            const float2 sc2 = make_float2(scale2, scale2);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int ql = c * 32 + e + u;
-              float p = ex2(fmaf(__uint_as_float(s[e + u]), scale2, -Ls[u]));
+            for (int u = 0; u < 4; u += 2) {
+              // two lanes at a time: arg = s*scale2 - lse2, dS = P * (dP - Delta)
+              const float2 arg = ffma2(make_float2(__uint_as_float(s[e + u]), __uint_as_float(s[e + u + 1])), sc2,
+                                       make_float2(-Ls[u], -Ls[u + 1]));
+              float2 p = make_float2(ex2(arg.x), ex2(arg.y));
               if (need_mask) {
+                const int ql = c * 32 + e + u;
                 const int qpos = q_lo + ql;
-                if (kv_pos > qpos || i * kTile + ql >= S_q || kv_pos >= S_kv) p = 0.f;
+                if (kv_pos > qpos || i * kTile + ql >= S_q || kv_pos >= S_kv) p.x = 0.f;
+                if (kv_pos > qpos + 1 || i * kTile + ql + 1 >= S_q || kv_pos >= S_kv) p.y = 0.f;
               }
-              pr[u] = p;
-              dr[u] = p * (__uint_as_float(dp[e + u]) - Ds[u]);
+              const float2 dd = fadd2(make_float2(__uint_as_float(dp[e + u]), __uint_as_float(dp[e + u + 1])),
+                                      make_float2(-Ds[u], -Ds[u + 1]));
+              const float2 ds = fmul2(p, dd);
+              pr[u] = p.x; pr[u + 1] = p.y;
+              dr[u] = ds.x; dr[u + 1] = ds.y;
             }
             pk[c2 * 16 + e / 2] = pack_bf16(pr[0], pr[1]);
             pk[c2 * 16 + e / 2 + 1] = pack_bf16(pr[2], pr[3]);

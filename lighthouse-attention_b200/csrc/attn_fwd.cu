@@ -249,23 +249,29 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         l *= alpha;
         m = mnew;
       }
-      float rsp[8];
+      // exponent arguments and row sums two lanes at a time (fma.rn.f32x2 / add.rn.f32x2)
+      float2 rsp[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) rsp[u] = 0.f;
+      for (int u = 0; u < 4; ++u) rsp[u] = make_float2(0.f, 0.f);
+      const float2 sc2 = make_float2(scale2, scale2), negm = make_float2(-m, -m);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t pk[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int i0 = h * 64 + 2 * e;
-          const float p0 = ex2(fmaf(__uint_as_float(s[i0 >> 5][i0 & 31]), scale2, -m));
-          const float p1 = ex2(fmaf(__uint_as_float(s[(i0 + 1) >> 5][(i0 + 1) & 31]), scale2, -m));
-          rsp[e & 7] += p0 + p1;
-          pk[e] = pack_bf16(p0, p1);
+          const float2 sv = make_float2(__uint_as_float(s[i0 >> 5][i0 & 31]),
+                                        __uint_as_float(s[(i0 + 1) >> 5][(i0 + 1) & 31]));
+          const float2 arg = ffma2(sv, sc2, negm);
+          const float2 pv = make_float2(ex2(arg.x), ex2(arg.y));
+          rsp[e & 3] = fadd2(rsp[e & 3], pv);
+          pk[e] = pack_bf16(pv.x, pv.y);
         }
         tmem_st32(lane_base + s_col + h * 32, pk);
       }
-      const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
+      const float2 r01 = fadd2(rsp[0], rsp[1]), r23 = fadd2(rsp[2], rsp[3]);
+      const float2 r = fadd2(r01, r23);
+      const float rs = r.x + r.y;
       tmem_st_wait();
       l += rs;
       tc_fence_before();

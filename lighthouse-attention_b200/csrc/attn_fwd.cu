@@ -218,15 +218,16 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        if (need_mask) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float v = __uint_as_float(s[c][e]);
-          if (need_mask) {
+          for (int e = 0; e < 32; ++e) {
             const int kvpos = j * kTile + c * 32 + e;
-            if (kvpos > qpos || kvpos >= S_kv) { v = -INFINITY; s[c][e] = __float_as_uint(v); }
+            if (kvpos > qpos || kvpos >= S_kv) s[c][e] = __float_as_uint(-INFINITY);
           }
-          mxp[e & 7] = fmaxf(mxp[e & 7], v);
         }
+#pragma unroll
+        for (int e = 0; e < 32; e += 2)
+          mxp[(e >> 1) & 7] = fmax3(mxp[(e >> 1) & 7], __uint_as_float(s[c][e]), __uint_as_float(s[c][e + 1]));
       }
       const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
                              fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));

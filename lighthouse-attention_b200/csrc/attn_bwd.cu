@@ -296,21 +296,22 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
       tc_fence_after();
       // dQ_i (TMEM lane = query row) -> swizzled fp32 stage -> TMA reduce-add into dQacc
+      uint32_t dqv[2][32];
+#pragma unroll
+      for (int c2 = 0; c2 < 2; ++c2) tmem_ld32(lane_base + kColDP + (2 * g + c2) * 32, dqv[c2]);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&sm->dq_free);                    // the MMA warp may overwrite these columns now
       if (tid == 0 && t > 0) bulk_wait_read_all();  // previous reduce has read the stage
       named_bar_sync(1, 256);
 #pragma unroll
       for (int c2 = 0; c2 < 2; ++c2) {
         const int c = 2 * g + c2;                   // this warp's 32-column chunk = stage box c
-        uint32_t v[32];
-        tmem_ld32(lane_base + kColDP + c * 32, v);
-        tmem_ld_wait();
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch)
           *reinterpret_cast<uint4*>(sdQ + c * kBox + r * 128 + ((ch ^ (r & 7)) << 4)) =
-              make_uint4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
+              make_uint4(dqv[c2][4 * ch], dqv[c2][4 * ch + 1], dqv[c2][4 * ch + 2], dqv[c2][4 * ch + 3]);
       }
-      tc_fence_before();
-      mbar_arrive(&sm->dq_free);
       fence_async_smem();
       named_bar_sync(1, 256);
       if (tid == 0) {

@@ -34,47 +34,56 @@ constexpr int kSelTopk = 128;
 constexpr int kSelHalf = 64;
 constexpr float kNegBig = -1e6f;   // placeholder score (reference :191-194, :227)
 
-// One comparator stage (k, j) of the descending bitonic network, branch-free.
+// Comparator stages of the descending bitonic network, branch-free.
 // NP = number of payload arrays moved with the key (1: index; 2: index + score).
+// Stages with j < 32 exchange across lanes (xor shuffles); k and j may be
+// run-time values there.
 template <int NP>
-__device__ __forceinline__ void bitonic_stage(int k, int j, int lane, float (&key)[4], float (&pf)[4],
+__device__ __forceinline__ void shuffle_stage(int k, int j, int lane, float (&key)[4], float (&pf)[4],
                                               int (&ix)[4]) {
-  if (j >= 32) {
-    const int rr = j >> 5;
+  // Integer predicates on purpose: the same logic written with bool ternaries
+  // compiles to a form about four times slower per stage on this target.
+  const int lower = (lane & j) == 0;
 #pragma unroll
-    for (int lo = 0; lo < 4; ++lo) {
-      if (lo & rr) continue;
-      const int hi = lo | rr;
-      const int i_lo = lane + 32 * lo;
-      const bool desc = (i_lo & k) == 0;
-      const float a = key[lo], b = key[hi];
-      const bool swap = desc ? (a < b) : (a > b);
-      key[lo] = swap ? b : a;
-      key[hi] = swap ? a : b;
-      const int ia = ix[lo], ib = ix[hi];
-      ix[lo] = swap ? ib : ia;
-      ix[hi] = swap ? ia : ib;
-      if (NP > 1) {
-        const float pa = pf[lo], pb = pf[hi];
-        pf[lo] = swap ? pb : pa;
-        pf[hi] = swap ? pa : pb;
-      }
-    }
-  } else {
-    const bool lower = (lane & j) == 0;
+  for (int r = 0; r < 4; ++r) {
+    const int i = lane + 32 * r;
+    const int desc = (i & k) == 0;
+    const float o = __shfl_xor_sync(0xffffffffu, key[r], j);
+    const int oi = __shfl_xor_sync(0xffffffffu, ix[r], j);
+    float op = 0.f;
+    if (NP > 1) op = __shfl_xor_sync(0xffffffffu, pf[r], j);
+    // lower partner keeps the larger value when descending; strict compares keep ties in place
+    const int lt = key[r] < o, gt = key[r] > o;
+    const int swap = (lower ^ desc) ? gt : lt;
+    key[r] = swap ? o : key[r];
+    ix[r] = swap ? oi : ix[r];
+    if (NP > 1) pf[r] = swap ? op : pf[r];
+  }
+}
+
+// Stages with j >= 32 exchange registers inside a thread; K and J are
+// compile-time so that the register indices are constants.
+template <int NP, int K, int J>
+__device__ __forceinline__ void register_stage(int lane, float (&key)[4], float (&pf)[4], int (&ix)[4]) {
+  constexpr int rr = J >> 5;
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int i = lane + 32 * r;
-      const bool desc = (i & k) == 0;
-      const float o = __shfl_xor_sync(0xffffffffu, key[r], j);
-      const int oi = __shfl_xor_sync(0xffffffffu, ix[r], j);
-      float op = 0.f;
-      if (NP > 1) op = __shfl_xor_sync(0xffffffffu, pf[r], j);
-      // lower partner keeps the larger value when descending; strict compares keep ties in place
-      const bool swap = (lower == desc) ? (key[r] < o) : (key[r] > o);
-      key[r] = swap ? o : key[r];
-      ix[r] = swap ? oi : ix[r];
-      if (NP > 1) pf[r] = swap ? op : pf[r];
+  for (int lo = 0; lo < 4; ++lo) {
+    if (lo & rr) continue;
+    const int hi = lo | rr;
+    const int i_lo = lane + 32 * lo;
+    const int desc = (i_lo & K) == 0;
+    const float a = key[lo], b = key[hi];
+    const int lt = a < b, gt = a > b;
+    const int swap = desc ? lt : gt;
+    key[lo] = swap ? b : a;
+    key[hi] = swap ? a : b;
+    const int ia = ix[lo], ib = ix[hi];
+    ix[lo] = swap ? ib : ia;
+    ix[hi] = swap ? ia : ib;
+    if (NP > 1) {
+      const float pa = pf[lo], pb = pf[hi];
+      pf[lo] = swap ? pb : pa;
+      pf[hi] = swap ? pa : pb;
     }
   }
 }
@@ -82,53 +91,38 @@ __device__ __forceinline__ void bitonic_stage(int k, int j, int lane, float (&ke
 struct SortSet2 { float key[4]; float pf[4]; int ix[4]; };   // qk sort: key qk, payload kq score + index
 struct SortSet1 { float key[4]; float pf[4]; int ix[4]; };   // kq sort: key kq, payload index
 
-// The (k, j) stage sequence is expanded at compile time so that every
-// register index and direction test in bitonic_stage is a constant.  The
-// dual form runs two independent networks stage by stage for twice the
-// instruction-level parallelism of a single warp.
-template <int K, int J, bool DUAL>
-struct BitonicStages {
-  static __device__ __forceinline__ void run(int lane, SortSet2& a, SortSet1& b) {
-    if (DUAL) bitonic_stage<2>(K, J, lane, a.key, a.pf, a.ix);
-    bitonic_stage<1>(K, J, lane, b.key, b.pf, b.ix);
-    BitonicStages<K, J / 2, DUAL>::run(lane, a, b);
-  }
-};
-template <int K, bool DUAL>
-struct BitonicStages<K, 0, DUAL> {
-  static __device__ __forceinline__ void run(int, SortSet2&, SortSet1&) {}
-};
-template <int K, bool DUAL>
-struct BitonicNet {
-  static __device__ __forceinline__ void run(int lane, SortSet2& a, SortSet1& b) {
-    BitonicNet<K / 2, DUAL>::run(lane, a, b);
-    BitonicStages<K, K / 2, DUAL>::run(lane, a, b);
-  }
-};
-template <bool DUAL>
-struct BitonicNet<1, DUAL> {
-  static __device__ __forceinline__ void run(int, SortSet2&, SortSet1&) {}
-};
+// The network as compact loops: stages with j < 32 take k and j at run time
+// (only the register index is unrolled); the three stages with j >= 32 are
+// spelled out.  A fully unrolled network is tens of KB of straight-line code
+// executed by one warp per SM, which stalls on instruction fetch.
+// NETS = 1: the kq set only; 2: the qk set only; 3: both, stage by stage
+// (two independent networks for instruction-level parallelism).
+template <int NETS>
+__device__ __forceinline__ void shuffle_stage2(int k, int j, int lane, SortSet2& a, SortSet1& b) {
+  if (NETS & 2) shuffle_stage<2>(k, j, lane, a.key, a.pf, a.ix);
+  if (NETS & 1) shuffle_stage<1>(k, j, lane, b.key, b.pf, b.ix);
+}
+template <int NETS, int K, int J>
+__device__ __forceinline__ void register_stage2(int lane, SortSet2& a, SortSet1& b) {
+  if (NETS & 2) register_stage<2, K, J>(lane, a.key, a.pf, a.ix);
+  if (NETS & 1) register_stage<1, K, J>(lane, b.key, b.pf, b.ix);
+}
 
-// qk network on a alone (the kq set is untouched): stages on a only.
-template <int K, int J>
-struct QkStages {
-  static __device__ __forceinline__ void run(int lane, SortSet2& a) {
-    bitonic_stage<2>(K, J, lane, a.key, a.pf, a.ix);
-    QkStages<K, J / 2>::run(lane, a);
+template <int NETS>
+__device__ __forceinline__ void bitonic128_sets(int lane, SortSet2& a, SortSet1& b) {
+#pragma unroll 1
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll 1
+    for (int j = k >> 1; j > 0; j >>= 1) shuffle_stage2<NETS>(k, j, lane, a, b);
   }
-};
-template <int K>
-struct QkStages<K, 0> { static __device__ __forceinline__ void run(int, SortSet2&) {} };
-template <int K>
-struct QkNet {
-  static __device__ __forceinline__ void run(int lane, SortSet2& a) {
-    QkNet<K / 2>::run(lane, a);
-    QkStages<K, K / 2>::run(lane, a);
-  }
-};
-template <>
-struct QkNet<1> { static __device__ __forceinline__ void run(int, SortSet2&) {} };
+  register_stage2<NETS, 64, 32>(lane, a, b);
+#pragma unroll 1
+  for (int j = 16; j > 0; j >>= 1) shuffle_stage2<NETS>(64, j, lane, a, b);
+  register_stage2<NETS, 128, 64>(lane, a, b);
+  register_stage2<NETS, 128, 32>(lane, a, b);
+#pragma unroll 1
+  for (int j = 16; j > 0; j >>= 1) shuffle_stage2<NETS>(128, j, lane, a, b);
+}
 
 struct SelGeom {
   int N, L, p, shift, T, ncc, S_tot, S_sel, chunk_len;
@@ -205,7 +199,7 @@ select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ s
     take();
     if (nb > 1) fetch(1);
     // qk sort of batch 0 (reference :203-232)
-    QkNet<kSelTopk>::run(lane, qk);
+    bitonic128_sets<2>(lane, qk, kq);
     for (int bt = 0; bt < nb; ++bt) {
       // kq set for batch bt: its top-64 and the qk rejects (reference :242-250)
 #pragma unroll
@@ -214,9 +208,9 @@ select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ s
         take();                                  // batch bt+1 joins the qk top-64
         if (bt + 2 < nb) fetch(bt + 2);
         // kq sort of batch bt and qk sort of batch bt+1 are independent: run them together
-        BitonicNet<kSelTopk, true>::run(lane, qk, kq);
+        bitonic128_sets<3>(lane, qk, kq);
       } else {
-        BitonicNet<kSelTopk, false>::run(lane, qk, kq);
+        bitonic128_sets<1>(lane, qk, kq);
       }
     }
     int tki[2], ix[2];

@@ -226,6 +226,77 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- model workload
+def run_model(args, rank, world, local_rank):
+    """270M Llama3-style training step (Lighthouse on 26 of 30
+    layers), bf16 autocast, AdamW, seq 65536, uniform random bytes; DDP over NCCL
+    for N > 1 (weak scaling: every rank trains on its own sequence)."""
+    import __graft_entry__ as ge
+    lh = ge.load_package()
+    from lighthouse_b200 import model as M
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    seq = args.seq_len or 65536
+    margs = M.ModelArgs(max_seq_len=seq)
+    torch.manual_seed(0)
+    model = M.Transformer(margs).to(dev)
+    model.init_weights(0)
+    if world > 1:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local_rank], bucket_cap_mb=100,
+                                                          gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
+    g = torch.Generator().manual_seed(1000 + rank)
+    host = [torch.randint(0, 256, (1, seq + 1), generator=g, dtype=torch.long).pin_memory() for _ in range(2)]
+    toks = [h.to(dev) for h in host]
+    for i in range(args.warmup):
+        M.train_step(model, opt, toks[i % 2])
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    with ClockSampler(local_rank) as clk:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(args.steps):
+            M.train_step(model, opt, toks[i % 2])
+        t1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    # end to end: tokens copied from pinned host memory each step, loss read back
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(1, min(args.steps, 3))
+    e0.record()
+    for i in range(e_steps):
+        loss = M.train_step(model, opt, host[i % 2].to(dev, non_blocking=True)).item()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+    assert lh._native.device_status() == 0
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    if rank != 0:
+        return
+    tokens = seq * world
+    n_layers_lh = sum(1 for i in range(margs.n_layers) if i not in margs.lighthouse_full_attn_layers)
+    line = {
+        "metric": "270M train tok/s (Lighthouse norm, k=2048, p=4, L=3)", "value": tokens / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 autocast, fp32 master",
+        "data": "synthetic (uniform random bytes, seeded)",
+        "config": {"workload": "llama3_270m_train_step", "params": M.num_params(model), "seq_len": seq,
+                   "global_batch": world, "lighthouse_layers": n_layers_lh, "parallelism": f"dp{world} (DDP/NCCL)",
+                   "l2": "activations far larger than L2"},
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": (seq + 1) * 8,
+                "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms, "final_loss": loss},
+        "gpu_launches": 10 * n_layers_lh * args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- CPU arm
 def cpu_sample(steps: int, warmup: int):
     """The reference path on the host cores, one head of the workload per step."""
@@ -275,10 +346,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="layer", choices=["layer", "model"],
+                    help="layer: BASELINE config 3 (default); model: config 4, the 270M training step")
     ap.add_argument("--seq-len", type=int, default=None, help="profiling only: override S")
     ap.add_argument("--topk", type=int, default=None, help="profiling only: override k")
     args = ap.parse_args()
-    if args.seq_len:
+    if args.seq_len and args.workload == "layer":
         CFG["S"] = args.seq_len
     if args.topk:
         CFG["k"] = args.topk
@@ -292,7 +365,10 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl")
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.workload == "model":
+            run_model(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

@@ -1,0 +1,161 @@
+"""Llama3-style model harness with Lighthouse layers.
+
+The reference trains a 270M Llama3 variant through a torchtitan patch
+(lighthouse-attention.patch): flavour at :283-296 (dim 1024, 30 layers,
+FFN hidden 1536, 8 heads, 8 KV heads, rope theta 1e4, byte vocabulary 256),
+the attention call site at :700-737 (q/k/v after RoPE in (B, S, H, D) go to
+the Lighthouse module, its (B, H, S, D) output is transposed back before wo)
+and full SDPA attention on layers [0, 1, 28, 29] (:754-766).  torchtitan at
+the patched revision is not available here, so this module restates that
+architecture in plain PyTorch with the package's Lighthouse layer in the
+attention of every other layer.
+
+Data parallelism is plain DDP over NCCL (gradient all-reduce, bucketed and
+overlapped with backward by torch).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .lighthouse_selection import lighthouse_attention
+
+
+@dataclass
+class ModelArgs:
+    """Field names follow the torchtitan TransformerModelArgs the patch extends
+    (lighthouse-attention.patch:551-579)."""
+    dim: int = 1024
+    n_layers: int = 30
+    n_heads: int = 8
+    n_kv_heads: int = 8
+    vocab_size: int = 256
+    hidden_dim: int = 1536
+    norm_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    max_seq_len: int = 65536
+    use_selection_lighthouse: bool = True
+    lighthouse_num_levels: int = 3
+    lighthouse_pooling_factor: int = 4
+    lighthouse_topk: int = 2048
+    lighthouse_scorer: str = "norm"
+    lighthouse_full_attn_layers: list = field(default_factory=lambda: [0, 1, 28, 29])
+
+
+def rope_freqs(head_dim: int, seq_len: int, theta: float, device) -> torch.Tensor:
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=device, dtype=torch.float32) / head_dim))
+    t = torch.arange(seq_len, device=device, dtype=torch.float32)
+    ang = torch.outer(t, inv)
+    return torch.polar(torch.ones_like(ang), ang)          # (S, D/2) complex64
+
+
+def apply_rope(x: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
+    """x (B, S, H, D); rotation of adjacent pairs as in the Llama3 reference model."""
+    xc = torch.view_as_complex(x.float().reshape(*x.shape[:-1], -1, 2))
+    out = torch.view_as_real(xc * freqs[None, :, None, :]).flatten(-2)
+    return out.to(x.dtype)
+
+
+class Attention(nn.Module):
+    def __init__(self, args: ModelArgs, layer_id: int):
+        super().__init__()
+        self.n_heads = args.n_heads
+        self.head_dim = args.dim // args.n_heads
+        if args.n_kv_heads != args.n_heads:
+            raise NotImplementedError("Lighthouse selection path requires n_kv_heads == n_heads")
+        self.wq = nn.Linear(args.dim, args.n_heads * self.head_dim, bias=False)
+        self.wk = nn.Linear(args.dim, args.n_heads * self.head_dim, bias=False)
+        self.wv = nn.Linear(args.dim, args.n_heads * self.head_dim, bias=False)
+        self.wo = nn.Linear(args.n_heads * self.head_dim, args.dim, bias=False)
+        self.lighthouse = args.use_selection_lighthouse and layer_id not in args.lighthouse_full_attn_layers
+        if self.lighthouse and args.lighthouse_scorer != "norm":
+            raise ValueError("only the `norm` Lighthouse scorer is provided")
+        self.L, self.p, self.k = args.lighthouse_num_levels, args.lighthouse_pooling_factor, args.lighthouse_topk
+
+    def forward(self, x, freqs):
+        B, S, _ = x.shape
+        xq = self.wq(x).view(B, S, self.n_heads, self.head_dim)
+        xk = self.wk(x).view(B, S, self.n_heads, self.head_dim)
+        xv = self.wv(x).view(B, S, self.n_heads, self.head_dim)
+        xq, xk = apply_rope(xq, freqs), apply_rope(xk, freqs)
+        if self.lighthouse:
+            out = lighthouse_attention(xq, xk, xv, self.L, self.p, self.k)          # (B, H, S, D)
+        else:
+            out = F.scaled_dot_product_attention(xq.transpose(1, 2), xk.transpose(1, 2), xv.transpose(1, 2),
+                                                 is_causal=True)
+        return self.wo(out.transpose(1, 2).reshape(B, S, -1))
+
+
+class FeedForward(nn.Module):
+    def __init__(self, dim: int, hidden: int):
+        super().__init__()
+        self.w1 = nn.Linear(dim, hidden, bias=False)
+        self.w2 = nn.Linear(hidden, dim, bias=False)
+        self.w3 = nn.Linear(dim, hidden, bias=False)
+
+    def forward(self, x):
+        return self.w2(F.silu(self.w1(x)) * self.w3(x))
+
+
+class Block(nn.Module):
+    def __init__(self, args: ModelArgs, layer_id: int):
+        super().__init__()
+        self.attention_norm = nn.RMSNorm(args.dim, eps=args.norm_eps)
+        self.attention = Attention(args, layer_id)
+        self.ffn_norm = nn.RMSNorm(args.dim, eps=args.norm_eps)
+        self.feed_forward = FeedForward(args.dim, args.hidden_dim)
+
+    def forward(self, x, freqs):
+        h = x + self.attention(self.attention_norm(x), freqs)
+        return h + self.feed_forward(self.ffn_norm(h))
+
+
+class Transformer(nn.Module):
+    def __init__(self, args: ModelArgs):
+        super().__init__()
+        self.args = args
+        self.tok_embeddings = nn.Embedding(args.vocab_size, args.dim)
+        self.layers = nn.ModuleList(Block(args, i) for i in range(args.n_layers))
+        self.norm = nn.RMSNorm(args.dim, eps=args.norm_eps)
+        self.output = nn.Linear(args.dim, args.vocab_size, bias=False)
+        self._freqs = None
+
+    def init_weights(self, seed: int = 0):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        for name, p in self.named_parameters():
+            if p.dim() == 2:
+                with torch.no_grad():
+                    p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+
+    def forward(self, tokens):
+        B, S = tokens.shape
+        if self._freqs is None or self._freqs.shape[0] < S or self._freqs.device != tokens.device:
+            self._freqs = rope_freqs(self.args.dim // self.args.n_heads, max(S, 1), self.args.rope_theta,
+                                     tokens.device)
+        freqs = self._freqs[:S]
+        h = self.tok_embeddings(tokens)
+        for layer in self.layers:
+            h = layer(h, freqs)
+        return self.output(self.norm(h))
+
+
+def num_params(model: nn.Module) -> int:
+    return sum(p.numel() for p in model.parameters())
+
+
+def train_step(model, optimizer, tokens: torch.Tensor) -> torch.Tensor:
+    """One next-byte-prediction step on tokens (B, S+1): inputs are the first S
+    bytes, labels the last S.  bf16 autocast over fp32 master weights (the
+    reference trains with bf16 mixed precision).  Returns the loss tensor."""
+    inputs, labels = tokens[:, :-1], tokens[:, 1:]
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        logits = model(inputs)
+    loss = F.cross_entropy(logits.float().reshape(-1, logits.shape[-1]), labels.reshape(-1))
+    loss.backward()
+    optimizer.step()
+    optimizer.zero_grad(set_to_none=True)
+    return loss.detach()

@@ -203,6 +203,16 @@ def run_ours(args, rank, world, local_rank):
     peak = peaks.get("bf16_tflops_sustained") or 1400.0
     peak_src = "measured sustained" if "bf16_tflops_sustained" in peaks else "fallback"
     achieved = bwd_flops / (bwd_ms * 1e-3) / 1e12
+    traffic = None
+    if (B, S, H, D, L, p, k) == (1, 131072, 8, 128, 3, 4, 2048):
+        # DRAM read + write of attn_bwd_kernel per launch from the committed ncu launch list
+        import re
+        try:
+            txt = open(os.path.join(ROOT, "profiles", "launches_layer_S131072_k2048.md")).read()
+            m = re.search(r"traffic_bytes_per_launch attn_bwd: (\d+)", txt)
+            traffic = int(m.group(1)) if m else None
+        except OSError:
+            pass
     tokens = B * S * world
     line = {
         "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
@@ -211,7 +221,7 @@ def run_ours(args, rank, world, local_rank):
         "config": _config({"parallelism": f"replicas x{world}"}),
         "roofline": {"kernel": "attn_bwd (prep + tcgen05 main + post)", "bound": "tensor",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                     "peak_source": peak_src, "traffic": None,
+                     "peak_source": peak_src, "traffic": traffic, "traffic_unit": "bytes per launch (ncu)",
                      "flops_per_launch": bwd_flops, "ms_per_launch": bwd_ms},
         "kernels": {"attn_fwd_ms": fwd_ms, "attn_fwd_tflops": fwd_flops / (fwd_ms * 1e-3) / 1e12,
                     "attn_bwd_ms": bwd_ms, "attn_bwd_tflops": achieved,

@@ -19,7 +19,8 @@ def _err(a, b):
 
 
 @pytest.mark.parametrize("shape", [(1, 4096, 2, 3, 4, 256), (1, 8192, 2, 3, 2, 256), (1, 16384, 2, 4, 2, 256),
-                                   (2, 8192, 2, 2, 8, 128)])
+                                   (2, 8192, 2, 2, 8, 128), (1, 8192, 3, 5, 2, 128), (1, 16384, 1, 3, 8, 128),
+                                   (3, 4096, 4, 3, 4, 128), (1, 24576, 2, 3, 4, 1536)])
 def test_lighthouse_local_fwd_bwd_vs_oracle(lh, O, cuda, shape):
     B, S, H, L, p, k = shape
     D = 128

@@ -7,19 +7,25 @@
 // Three launches:
 //   1. prep:  Delta[q] = sum_d dO[q,d] * O[q,d] (fp32), dQacc = 0
 //   2. main:  one CTA per (128-key tile j, b*h); K_j and V_j stay in shared
-//             memory while the CTA walks every query tile i that can see them:
-//               S^T  = K_j Q_i^T             (SS, TMEM cols   0..127)
-//               dP^T = V_j dO_i^T            (SS, TMEM cols 128..255)
-//             softmax warps (one key row per thread = TMEM lane):
-//               P^T  = exp2(S^T * scale*log2e - lse2[q])  -> bf16 into TMEM cols 0..63
-//               dS^T = P^T * (dP^T - Delta[q])            -> bf16 into shared memory
-//               dV_j += P^T dO_i             (TS, TMEM cols 256..383)
-//               dK_j += dS^T Q_i             (SS, TMEM cols 384..511)
-//               dQ_i  = dS K_j               (SS, dS read MN-major; TMEM cols 128..255)
-//             the softmax warps then move dQ_i from TMEM into a swizzled fp32
-//             shared-memory stage that a TMA reduce-add adds into dQacc.  Eight compute warps: two per TMEM lane
-//             quadrant, each owning 64 of the 128 columns.  At the end dK (times scale) and dV are
-//             written as bf16.
+//             memory while the CTA walks every query tile i that can see them.
+//             Each query tile is handled as two 64-query halves h so that the
+//             elementwise work on one half overlaps the MMAs of the other:
+//               S^T_h  = K_j Q_h^T            (SS, N = 64, TMEM cols  64h..)
+//               dP^T_h = V_j dO_h^T           (SS, N = 64, TMEM cols 128 + 64h..)
+//             compute warps (one key row per thread = TMEM lane, 32 queries each):
+//               P^T  = exp2(S^T * scale*log2e - lse2[q])
+//               dS^T = P^T * (dP^T - Delta[q])
+//             both as bf16 pairs back into the warp's own S^T columns, and dS^T
+//             also into shared memory;
+//               dV_j += P^T_h dO_h            (TS, TMEM cols 256..383)
+//               dK_j += dS^T_h Q_h            (TS, TMEM cols 384..511)
+//               dQ_i^T = K_j^T dS_i^T         (SS, both MN-major; TMEM cols 128..255)
+//             a drain warpgroup reads dQ_i^T (TMEM lane = head dimension) and
+//             adds it into the fp32 dQacc with coalesced red.global.add: no
+//             shared-memory stage, so shared-memory bandwidth (which the SS
+//             MMAs saturate) is left to the MMAs and the Q / dO refills, and the
+//             freed 64 KB double-buffers Q_i / dO_i.  At the end dK (times
+//             scale) and dV are written as bf16.
 //   3. post:  dQ = bf16(dQacc * scale)
 // Shared-memory operands use the 128-byte swizzle; Q_i / dO_i / K_j / V_j
 // arrive by TMA (no multicast).  Every mbarrier wait is bounded.
@@ -35,21 +41,25 @@ namespace lh {
 using namespace sm100;
 
 __device__ int g_attn_bwd_status;   // set to 1 when a bounded wait gave up
-int make_tmap_rows(CUtensorMap* m, const void* ptr, int rows, int BH);
-int make_tmap_rows_f32(CUtensorMap* m, const void* ptr, int rows, int BH);
+int make_tmap_rows(CUtensorMap* m, const void* ptr, int rows, int BH, int box_rows);
 
 namespace bwd {
 constexpr int kTile = 128;
 constexpr int kD = 128;
 constexpr int kBox = 16384;
 constexpr int kTileBytes = 2 * kBox;
-constexpr int kThreads = 384;   // {producer, MMA, 2 idle}, then 8 compute warps (2 per TMEM lane quadrant)
+// warpgroup 0: {TMA producer, MMA issuer, 2 idle}; warpgroup 1: dQ drain;
+// warpgroups 2-3: P / dS (two warps per TMEM lane quadrant)
+constexpr int kThreads = 512;
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384, kTmemCols = 512;
-constexpr int kDqStageBytes = 4 * kBox;   // 128 x 128 fp32
+constexpr int kStages = 2;                 // Q_i / dO_i buffers
 }  // namespace bwd
 
 struct BwdSmem {
-  uint64_t kv_full, q_full, q_empty, s_ready, p_ready, dq_ready, dq_free;
+  uint64_t kv_full, dq_ready, mma_done;
+  uint64_t dq_free[2];                                           // dQ^T query columns [64h, 64h+64) read
+  uint64_t q_full[bwd::kStages][2], q_empty[bwd::kStages][2];   // per stage and 64-query half
+  uint64_t s_ready[2], p_ready[2];                               // per 64-query half
   uint32_t tmem_base;
   int abort;
   float lse2[2][bwd::kTile];
@@ -62,6 +72,9 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+__device__ __forceinline__ void red_add_f32(float* p, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
 
 // 16-byte store of 8 bf16 into the SW128 K-major layout of a 128 x 128 tile
 // stored as two 64-column boxes: row r, columns [8c, 8c+8).
@@ -73,22 +86,20 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int r, int c, uint4 v) {
 __global__ void __launch_bounds__(bwd::kThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                const __grid_constant__ CUtensorMap tmdQ,
-                const float* __restrict__ LSE, const float* __restrict__ Delta,
+                const float* __restrict__ LSE, const float* __restrict__ Delta, float* __restrict__ dQacc,
                 __nv_bfloat16* __restrict__ dK, __nv_bfloat16* __restrict__ dV, int S_q, int S_kv, int q_off,
                 float scale2, float scale) {
   using namespace bwd;
-  // 5 bf16 tiles + the fp32 dQ stage + barriers fill 227 KB: no room for
-  // alignment slack, so the dynamic window itself must be 1024-byte aligned.
+  // 7 bf16 tiles + barriers fill 227 KB: no room for alignment slack, so the
+  // dynamic window itself must be 1024-byte aligned.
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = smem_raw;
   uint8_t* sK = base;
   uint8_t* sV = base + kTileBytes;
-  uint8_t* sQ = base + 2 * kTileBytes;
-  uint8_t* sdO = base + 3 * kTileBytes;
-  uint8_t* sdS = base + 4 * kTileBytes;
-  uint8_t* sdQ = base + 5 * kTileBytes;          // fp32 dQ_i stage: 4 boxes of 128 rows x 32 floats, SW128
-  BwdSmem* sm = reinterpret_cast<BwdSmem*>(base + 5 * kTileBytes + kDqStageBytes);
+  uint8_t* sQ = base + 2 * kTileBytes;                  // kStages tiles
+  uint8_t* sdO = base + (2 + kStages) * kTileBytes;     // kStages tiles
+  uint8_t* sdS = base + (2 + 2 * kStages) * kTileBytes;
+  BwdSmem* sm = reinterpret_cast<BwdSmem*>(base + (3 + 2 * kStages) * kTileBytes);
 
   const int bh = blockIdx.x;
   const int j = blockIdx.y;                      // key tile (heaviest first: j = 0 sees every query)
@@ -105,12 +116,17 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   if (threadIdx.x == 0) {
     mbar_init(&sm->kv_full, 1);
-    mbar_init(&sm->q_full, 1);
-    mbar_init(&sm->q_empty, 1);
-    mbar_init(&sm->s_ready, 1);
-    mbar_init(&sm->p_ready, 256);
     mbar_init(&sm->dq_ready, 1);
-    mbar_init(&sm->dq_free, 256);
+    mbar_init(&sm->mma_done, 1);
+    for (int h = 0; h < 2; ++h) {
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(&sm->q_full[s][h], 1);
+        mbar_init(&sm->q_empty[s][h], 1);
+      }
+      mbar_init(&sm->s_ready[h], 1);
+      mbar_init(&sm->p_ready[h], 256);
+      mbar_init(&sm->dq_free[h], 128);
+    }
     sm->abort = 0;
     fence_mbar_init();
   }
@@ -122,100 +138,197 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   volatile int* abort = &sm->abort;
 
   if (warp < 4) {
-  // Warpgroup 0 hands registers to the compute warpgroups: 96 + 2 x 200 per
-  // thread-slot stays within the 3 x 168 of the launch (one aligned setmaxnreg per warpgroup).
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 96;\n" ::: "memory");
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && n_it > 0) {
-      mbar_expect_tx(&sm->kv_full, 2 * kTileBytes);
-      tma_load_3d(sK, &tmK, &sm->kv_full, 0, j * kTile, bh);
-      tma_load_3d(sK + kBox, &tmK, &sm->kv_full, 64, j * kTile, bh);
-      tma_load_3d(sV, &tmV, &sm->kv_full, 0, j * kTile, bh);
-      tma_load_3d(sV + kBox, &tmV, &sm->kv_full, 64, j * kTile, bh);
-    }
-    for (int t = 0; t < n_it; ++t) {
-      if (t > 0) {
-        bool ok = mbar_wait(&sm->q_empty, (t - 1) & 1, abort);
-        if (__any_sync(0xffffffffu, !ok)) break;
+    // Register split 112 (this warpgroup) + 128 (drain) + 2 x 136 (P / dS) per
+    // thread-slot equals the 4 x 128 of the launch (one aligned setmaxnreg per
+    // warpgroup; .inc may not go below the launch's 128, .dec not above it).
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 112;\n" ::: "memory");
+    if (warp == 0) {
+      // ---------------------------------------------------------- TMA producer
+      if (lane == 0 && n_it > 0) {
+        mbar_expect_tx(&sm->kv_full, 2 * kTileBytes);
+        tma_load_3d(sK, &tmK, &sm->kv_full, 0, j * kTile, bh);
+        tma_load_3d(sK + kBox, &tmK, &sm->kv_full, 64, j * kTile, bh);
+        tma_load_3d(sV, &tmV, &sm->kv_full, 0, j * kTile, bh);
+        tma_load_3d(sV + kBox, &tmV, &sm->kv_full, 64, j * kTile, bh);
       }
-      if (lane == 0) {
-        const int i = i0 + t;
-        mbar_expect_tx(&sm->q_full, 2 * kTileBytes);
-        tma_load_3d(sQ, &tmQ, &sm->q_full, 0, i * kTile, bh);
-        tma_load_3d(sQ + kBox, &tmQ, &sm->q_full, 64, i * kTile, bh);
-        tma_load_3d(sdO, &tmdO, &sm->q_full, 0, i * kTile, bh);
-        tma_load_3d(sdO + kBox, &tmdO, &sm->q_full, 64, i * kTile, bh);
-      }
-      __syncwarp();
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t id_kk = idesc_bf16_f32(kTile, kTile, false, false);   // A K-major, B K-major
-    constexpr uint32_t id_kmn = idesc_bf16_f32(kTile, kD, false, true);      // A K-major, B MN-major
-    constexpr uint32_t id_mnmn = idesc_bf16_f32(kTile, kD, true, true);      // A MN-major, B MN-major
-    const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO),
-                   adS = smem_u32(sdS);
-    bool ok = n_it > 0 ? mbar_wait(&sm->kv_full, 0, abort) : true;
-    for (int t = 0; t < n_it; ++t) {
-      ok = ok && mbar_wait(&sm->q_full, t & 1, abort);
-      if (__any_sync(0xffffffffu, !ok)) break;
-      tc_fence_after();
-      if (lane == 0) {
-        // S^T: the S columns are free (P_{i-1} was read by the dV MMA already issued)
+      // Q_i and dO_i arrive in two 64-row halves into a ring of kStages tiles;
+      // each half is refilled once the dV / dK MMAs of that half have read it.
+      bool ok = true;
+      for (int t = 0; t < n_it && ok; ++t) {
+        const int i = i0 + t, st = t % kStages;
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-          mma_ss(tbase + kColS, smem_desc_sw128(aK + off, 16, 1024), smem_desc_sw128(aQ + off, 16, 1024), id_kk,
-                 kk > 0);
+        for (int h = 0; h < 2; ++h) {
+          if (t >= kStages) ok = mbar_wait(&sm->q_empty[st][h], ((t / kStages) - 1) & 1, abort);
+          if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+          if (lane == 0) {
+            const int row = i * kTile + h * 64;
+            uint8_t* q = sQ + st * kTileBytes + h * (kBox / 2);
+            uint8_t* d = sdO + st * kTileBytes + h * (kBox / 2);
+            mbar_expect_tx(&sm->q_full[st][h], kTileBytes);
+            tma_load_3d(q, &tmQ, &sm->q_full[st][h], 0, row, bh);
+            tma_load_3d(q + kBox, &tmQ, &sm->q_full[st][h], 64, row, bh);
+            tma_load_3d(d, &tmdO, &sm->q_full[st][h], 0, row, bh);
+            tma_load_3d(d + kBox, &tmdO, &sm->q_full[st][h], 64, row, bh);
+          }
+          __syncwarp();
         }
       }
-      __syncwarp();
-      // dP^T reuses the columns of dQ_{i-1}: wait until the compute warps have read it
-      if (t > 0) ok = mbar_wait(&sm->dq_free, (t - 1) & 1, abort);
-      if (__any_sync(0xffffffffu, !ok)) break;
-      tc_fence_after();
-      if (lane == 0) {
+    } else if (warp == 1 || warp == 2) {
+      // ---------------------------------------------------------- MMA issuers
+      // Two issuing warps so that the tensor pipe stays fed while one of them
+      // waits: its instruction queue is shallow, and a wait of the issuing
+      // thread (even on a barrier that has already completed) leaves the pipe
+      // idle for a shared-memory round trip.  Warp 1 issues S^T / dP^T, warp 2
+      // dV / dK and dQ^T.  tcgen05.commit tracks the committing thread's own
+      // MMAs, and every TMEM / shared-memory hazard between the two warps is
+      // covered by a barrier below.
+      constexpr uint32_t id_s = idesc_bf16_f32(kTile, 64, false, false);     // S^T / dP^T halves: N = 64 queries
+      constexpr uint32_t id_kmn = idesc_bf16_f32(kTile, kD, false, true);    // A K-major (TMEM), B MN-major
+      constexpr uint32_t id_mnmn = idesc_bf16_f32(kD, kTile, true, true);    // dQ^T: A MN-major, B MN-major
+      // Descriptors are a per-operand base plus a constant offset (the start
+      // address field holds addr >> 4 in its low 14 bits and every shared
+      // address is below 256 KB, so the add cannot carry out of the field).
+      // The empty asm keeps the compiler from hoisting every per-k descriptor
+      // out of the tile loop, which would not fit this warpgroup's registers.
+      auto kdesc = [](uint32_t addr) {            // K-major: lbo 16, sbo 1024
+        uint64_t d = smem_desc_sw128(addr, 16, 1024);
+        asm volatile("" : "+l"(d));
+        return d;
+      };
+      auto mdesc = [](uint32_t addr) {            // MN-major: lbo = box stride, sbo 1024
+        uint64_t d = smem_desc_sw128(addr, kBox, 1024);
+        asm volatile("" : "+l"(d));
+        return d;
+      };
+      auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        const bool ok = mbar_wait(bar, parity, abort);
+        if (__any_sync(0xffffffffu, !ok)) return false;
+        tc_fence_after();
+        return true;
+      };
+      bool ok = true;
+      if (warp == 1) {
+        // S^T_h and dP^T_h of tile t.  S^T_h overwrites P^T_h / dS^T_h of tile
+        // t-1 (read by warp 2's dV / dK MMAs, complete when q_empty of that
+        // half commits); dP^T_h overwrites half h of dQ^T of tile t-1 (read by
+        // the drain warps, dq_free[h]).
+        const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+        ok = n_it > 0 ? wait(&sm->kv_full, 0) : true;
+        for (int t = 0; t < n_it && ok; ++t) {
+          const int st = t % kStages;
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-          mma_ss(tbase + kColDP, smem_desc_sw128(aV + off, 16, 1024), smem_desc_sw128(adO + off, 16, 1024), id_kk,
-                 kk > 0);
+          for (int h = 0; h < 2; ++h) {
+            ok = wait(&sm->q_full[st][h], (t / kStages) & 1);
+            if (ok && t > 0) ok = wait(&sm->q_empty[(t - 1) % kStages][h], ((t - 1) / kStages) & 1);
+            if (!ok) break;
+            if (lane == 0) {
+              const uint64_t da = kdesc(aK), db = kdesc(smem_u32(sQ + st * kTileBytes) + h * (kBox / 2));
+#pragma unroll
+              for (int kk = 0; kk < kD / 16; ++kk) {
+                const uint32_t off = ((kk >> 2) * kBox + (kk & 3) * 32) >> 4;
+                mma_ss(tbase + kColS + h * 64, da + off, db + off, id_s, kk > 0);
+              }
+            }
+            __syncwarp();
+            if (t > 0) ok = wait(&sm->dq_free[h], (t - 1) & 1);
+            if (!ok) break;
+            if (lane == 0) {
+              const uint64_t da = kdesc(aV), db = kdesc(smem_u32(sdO + st * kTileBytes) + h * (kBox / 2));
+#pragma unroll
+              for (int kk = 0; kk < kD / 16; ++kk) {
+                const uint32_t off = ((kk >> 2) * kBox + (kk & 3) * 32) >> 4;
+                mma_ss(tbase + kColDP + h * 64, da + off, db + off, id_s, kk > 0);
+              }
+              mma_commit(&sm->s_ready[h]);
+            }
+            __syncwarp();
+          }
         }
-        mma_commit(&sm->s_ready);
-      }
-      __syncwarp();
-      ok = mbar_wait(&sm->p_ready, t & 1, abort);
-      if (__any_sync(0xffffffffu, !ok)) break;
-      tc_fence_after();
-      if (lane == 0) {
+      } else {
+        // dV += P^T_h dO_h and dK += dS^T_h Q_h with A operands from TMEM:
+        // compute warp w of a quadrant leaves the bf16 pairs of its 32 queries
+        // of half h at columns [64h + 32w, +16) (P^T) and [64h + 32w + 16, +16)
+        // (dS^T).  dQ_i^T = K^T dS^T goes first after the second half.
+        const uint32_t aK = smem_u32(sK), adS = smem_u32(sdS);
+        for (int t = 0; t < n_it && ok; ++t) {
+          const int st = t % kStages;
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk)   // dV += P^T dO   (K = query rows)
-          mma_ts(tbase + kColDV, tbase + kColS + kk * 8, smem_desc_sw128(adO + kk * 2048, kBox, 1024), id_kmn,
-                 (t > 0 || kk > 0) ? 1u : 0u);
+          for (int h = 0; h < 2; ++h) {
+            ok = wait(&sm->p_ready[h], t & 1);
+            if (!ok) break;
+            if (lane == 0) {
+              if (h == 1) {
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {  // dK += dS^T Q
-          const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-          mma_ss(tbase + kColDK, smem_desc_sw128(adS + off, 16, 1024), smem_desc_sw128(aQ + kk * 2048, kBox, 1024),
-                 id_kmn, (t > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < kTile / 16; ++kk) {    // dQ_i^T = K^T dS^T   (K = key rows)
+                  const uint64_t da = mdesc(aK), db = mdesc(adS);
+                  mma_ss(tbase + kColDP, da + ((kk * 2048) >> 4), db + ((kk * 2048) >> 4), id_mnmn, kk > 0);
+                }
+                mma_commit(&sm->dq_ready);
+              }
+              const uint64_t dq = mdesc(smem_u32(sQ + st * kTileBytes) + h * 4 * 2048);
+              const uint64_t ddo = mdesc(smem_u32(sdO + st * kTileBytes) + h * 4 * 2048);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t a = tbase + kColS + h * 64 + (kk >> 1) * 32 + (kk & 1) * 8;
+                const uint32_t acc = (t > 0 || h > 0 || kk > 0) ? 1u : 0u;
+                mma_ts(tbase + kColDV, a, ddo + ((kk * 2048) >> 4), id_kmn, acc);
+                mma_ts(tbase + kColDK, a + 16, dq + ((kk * 2048) >> 4), id_kmn, acc);
+              }
+              mma_commit(&sm->q_empty[st][h]);   // Q_h / dO_h of this stage and P^T_h / dS^T_h no longer read
+            }
+            __syncwarp();
+          }
         }
-        mma_commit(&sm->q_empty);                 // Q_i / dO_i no longer read: fetch the next tile
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk)    // dQ_i = dS K   (K = key rows)
-          mma_ss(tbase + kColDP, smem_desc_sw128(adS + kk * 2048, kBox, 1024),
-                 smem_desc_sw128(aK + kk * 2048, kBox, 1024), id_mnmn, kk > 0);
-        mma_commit(&sm->dq_ready);
+        if (lane == 0) mma_commit(&sm->mma_done);   // every dV / dK MMA of this CTA has completed
+        __syncwarp();
       }
-      __syncwarp();
     }
-  }
+  } else if (warp < 8) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 128;\n" ::: "memory");
+    // ------------------------------------------------------------ dQ drain
+    // TMEM lane = head-dimension column d; each thread adds its d of all 128
+    // query rows: a warp's red.global.add covers one 128-byte row segment.
+    const int quad = warp & 3;
+    const int d = quad * 32 + lane;
+    const uint32_t lane_base = tbase + ((uint32_t)(quad * 32) << 16);
+    bool ok = true;
+    for (int t = 0; t < n_it && ok; ++t) {
+      const int i = i0 + t;
+      ok = mbar_wait(&sm->dq_ready, t & 1, abort);
+      if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+      tc_fence_after();
+      float* dst = dQacc + ((size_t)bh * S_q + (size_t)i * kTile) * kD + d;
+      const int rows = S_q - i * kTile < kTile ? S_q - i * kTile : kTile;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {               // query rows [64h, 64h+64)
+        uint32_t v[2][32];
+        tmem_ld32(lane_base + kColDP + h * 64, v[0]);
+        tmem_ld32(lane_base + kColDP + h * 64 + 32, v[1]);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&sm->dq_free[h]);             // the MMA warp may overwrite these columns now
+        float* p = dst + (size_t)(h * 64) * kD;
+        if (rows == kTile) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) red_add_f32(p + (size_t)(c * 32 + e) * kD, __uint_as_float(v[c][e]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (h * 64 + c * 32 + e < rows) red_add_f32(p + (size_t)(c * 32 + e) * kD, __uint_as_float(v[c][e]));
+        }
+      }
+    }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
-    // ------------------------------------------------------------ softmax / dS / drain
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 136;\n" ::: "memory");
+    // ------------------------------------------------------------ P / dS
     const int quad = warp & 3;
     const int r = quad * 32 + lane;                 // key row inside the tile (TMEM lane)
-    const int tid = threadIdx.x - 128;              // 0..255
-    const int g = tid >> 7;                         // column half: query columns / d columns [64g, 64g+64)
+    const int tid = threadIdx.x - 256;              // 0..255
+    const int g = tid >> 7;                         // which 32 queries of each half
     const int kv_pos = j * kTile + r;
     const uint32_t lane_base = tbase + ((uint32_t)(quad * 32) << 16);
     bool ok = true;
@@ -228,100 +341,66 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         sm->delta[buf][tid] = q < S_q ? Delta[(size_t)bh * S_q + q] : 0.f;
       }
       named_bar_sync(1, 256);
-      ok = mbar_wait(&sm->s_ready, t & 1, abort);
-      if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
-      tc_fence_after();
       const int q_lo = q_off + i * kTile;
       const bool need_mask = (j * kTile + kTile - 1 > q_lo) || (i * kTile + kTile > S_q) || (j * kTile + kTile > S_kv);
-      {
-        const int h = g;                            // this warp's 64 query columns
-        uint32_t pk[32];
-        // both 32-column chunks of S and dP in flight before a single wait
-        uint32_t s2[2][32], dp2[2][32];
-#pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          tmem_ld32(lane_base + kColS + (h * 2 + c2) * 32, s2[c2]);
-          tmem_ld32(lane_base + kColDP + (h * 2 + c2) * 32, dp2[c2]);
-        }
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        ok = mbar_wait(&sm->s_ready[h], t & 1, abort);
+        if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+        tc_fence_after();
+        const int qc0 = h * 64 + g * 32;            // this warp's 32 query columns
+        uint32_t s[32], dp[32], pk[16], dsw[16];
+        tmem_ld32(lane_base + kColS + qc0, s);
+        tmem_ld32(lane_base + kColDP + qc0, dp);
         tmem_ld_wait();
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          const int c = h * 2 + c2;                 // 32-column chunk
-          const uint32_t (&s)[32] = s2[c2];
-          const uint32_t (&dp)[32] = dp2[c2];
-          uint32_t dsw[16];
+        for (int e = 0; e < 32; e += 4) {
+          const float4 L4 = *reinterpret_cast<const float4*>(&sm->lse2[buf][qc0 + e]);
+          const float4 D4 = *reinterpret_cast<const float4*>(&sm->delta[buf][qc0 + e]);
+          const float Ls[4] = {L4.x, L4.y, L4.z, L4.w};
+          const float Ds[4] = {D4.x, D4.y, D4.z, D4.w};
+          float pr[4], dr[4];
+          const float2 sc2 = make_float2(scale2, scale2);
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            const float4 L4 = *reinterpret_cast<const float4*>(&sm->lse2[buf][c * 32 + e]);
-            const float4 D4 = *reinterpret_cast<const float4*>(&sm->delta[buf][c * 32 + e]);
-            const float Ls[4] = {L4.x, L4.y, L4.z, L4.w};
-            const float Ds[4] = {D4.x, D4.y, D4.z, D4.w};
-            float pr[4], dr[4];
-            const float2 sc2 = make_float2(scale2, scale2);
-#pragma unroll
-            for (int u = 0; u < 4; u += 2) {
-              // two lanes at a time: arg = s*scale2 - lse2, dS = P * (dP - Delta)
-              const float2 arg = ffma2(make_float2(__uint_as_float(s[e + u]), __uint_as_float(s[e + u + 1])), sc2,
-                                       make_float2(-Ls[u], -Ls[u + 1]));
-              float2 p = make_float2(ex2(arg.x), ex2(arg.y));
-              if (need_mask) {
-                const int ql = c * 32 + e + u;
-                const int qpos = q_lo + ql;
-                if (kv_pos > qpos || i * kTile + ql >= S_q || kv_pos >= S_kv) p.x = 0.f;
-                if (kv_pos > qpos + 1 || i * kTile + ql + 1 >= S_q || kv_pos >= S_kv) p.y = 0.f;
-              }
-              const float2 dd = fadd2(make_float2(__uint_as_float(dp[e + u]), __uint_as_float(dp[e + u + 1])),
-                                      make_float2(-Ds[u], -Ds[u + 1]));
-              const float2 ds = fmul2(p, dd);
-              pr[u] = p.x; pr[u + 1] = p.y;
-              dr[u] = ds.x; dr[u + 1] = ds.y;
+          for (int u = 0; u < 4; u += 2) {
+            // two lanes at a time: arg = s*scale2 - lse2, dS = P * (dP - Delta)
+            const float2 arg = ffma2(make_float2(__uint_as_float(s[e + u]), __uint_as_float(s[e + u + 1])), sc2,
+                                     make_float2(-Ls[u], -Ls[u + 1]));
+            float2 p = make_float2(ex2(arg.x), ex2(arg.y));
+            if (need_mask) {
+              const int ql = qc0 + e + u;
+              const int qpos = q_lo + ql;
+              if (kv_pos > qpos || i * kTile + ql >= S_q || kv_pos >= S_kv) p.x = 0.f;
+              if (kv_pos > qpos + 1 || i * kTile + ql + 1 >= S_q || kv_pos >= S_kv) p.y = 0.f;
             }
-            pk[c2 * 16 + e / 2] = pack_bf16(pr[0], pr[1]);
-            pk[c2 * 16 + e / 2 + 1] = pack_bf16(pr[2], pr[3]);
-            dsw[e / 2] = pack_bf16(dr[0], dr[1]);
-            dsw[e / 2 + 1] = pack_bf16(dr[2], dr[3]);
+            const float2 dd = fadd2(make_float2(__uint_as_float(dp[e + u]), __uint_as_float(dp[e + u + 1])),
+                                    make_float2(-Ds[u], -Ds[u + 1]));
+            const float2 ds = fmul2(p, dd);
+            pr[u] = p.x; pr[u + 1] = p.y;
+            dr[u] = ds.x; dr[u + 1] = ds.y;
           }
-#pragma unroll
-          for (int v = 0; v < 4; ++v)
-            st_sw128(sdS, r, c * 4 + v, make_uint4(dsw[4 * v], dsw[4 * v + 1], dsw[4 * v + 2], dsw[4 * v + 3]));
+          pk[e / 2] = pack_bf16(pr[0], pr[1]);
+          pk[e / 2 + 1] = pack_bf16(pr[2], pr[3]);
+          dsw[e / 2] = pack_bf16(dr[0], dr[1]);
+          dsw[e / 2 + 1] = pack_bf16(dr[2], dr[3]);
         }
-        tmem_st32(lane_base + kColS + h * 32, pk);
-      }
-      tmem_st_wait();
-      fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(&sm->p_ready);
-      // drain dQ_i: TMEM lane = query row
-      ok = mbar_wait(&sm->dq_ready, t & 1, abort);
-      if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
-      tc_fence_after();
-      // dQ_i (TMEM lane = query row) -> swizzled fp32 stage -> TMA reduce-add into dQacc
-      uint32_t dqv[2][32];
 #pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) tmem_ld32(lane_base + kColDP + (2 * g + c2) * 32, dqv[c2]);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&sm->dq_free);                    // the MMA warp may overwrite these columns now
-      if (tid == 0 && t > 0) bulk_wait_read_all();  // previous reduce has read the stage
-      named_bar_sync(1, 256);
-#pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        const int c = 2 * g + c2;                   // this warp's 32-column chunk = stage box c
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch)
-          *reinterpret_cast<uint4*>(sdQ + c * kBox + r * 128 + ((ch ^ (r & 7)) << 4)) =
-              make_uint4(dqv[c2][4 * ch], dqv[c2][4 * ch + 1], dqv[c2][4 * ch + 2], dqv[c2][4 * ch + 3]);
-      }
-      fence_async_smem();
-      named_bar_sync(1, 256);
-      if (tid == 0) {
-#pragma unroll
-        for (int b = 0; b < 4; ++b) tma_reduce_add_3d(&tmdQ, sdQ + b * kBox, 32 * b, i * kTile, bh);
-        bulk_commit();
+        for (int v = 0; v < 4; ++v)
+          st_sw128(sdS, r, qc0 / 8 + v, make_uint4(dsw[4 * v], dsw[4 * v + 1], dsw[4 * v + 2], dsw[4 * v + 3]));
+        // P^T and dS^T as bf16 pairs into this warp's own 32 S^T columns (no
+        // other warp reads them), where the dV / dK MMAs take them as A
+        tmem_st16(lane_base + kColS + qc0, pk);
+        tmem_st16(lane_base + kColS + qc0 + 16, dsw);
+        tmem_st_wait();
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(&sm->p_ready[h]);
       }
     }
-    if (tid == 0) bulk_wait_all();
-    // epilogue: dV and dK rows of this key tile
+    // epilogue: dV and dK rows of this key tile, once every MMA has completed
+    if (!__any_sync(0xffffffffu, !ok)) {
+      ok = n_it > 0 ? mbar_wait(&sm->mma_done, 0, abort) : true;
+    }
     if (!__any_sync(0xffffffffu, !ok)) {
       tc_fence_after();
 #pragma unroll
@@ -423,22 +502,20 @@ int attn_bwd(const void* q, const void* k, const void* v, const void* o, const f
   float* Delta = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + align256(rows * D * sizeof(float)));
   CUtensorMap mq, mk, mv, mdo;
   int rc;
-  if ((rc = make_tmap_rows(&mq, q, S_q, B * H))) return rc;
-  if ((rc = make_tmap_rows(&mk, k, S_kv, B * H))) return rc;
-  if ((rc = make_tmap_rows(&mv, v, S_kv, B * H))) return rc;
-  if ((rc = make_tmap_rows(&mdo, dO, S_q, B * H))) return rc;
-  CUtensorMap mdq;
-  if ((rc = make_tmap_rows_f32(&mdq, dQacc, S_q, B * H))) return rc;
+  if ((rc = make_tmap_rows(&mq, q, S_q, B * H, 64))) return rc;
+  if ((rc = make_tmap_rows(&mk, k, S_kv, B * H, 128))) return rc;
+  if ((rc = make_tmap_rows(&mv, v, S_kv, B * H, 128))) return rc;
+  if ((rc = make_tmap_rows(&mdo, dO, S_q, B * H, 64))) return rc;
   {
     const long long threads = (long long)rows * 32;
     attn_bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
         (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, Delta, dQacc, (long long)rows);
     if ((rc = check_launch("attn_bwd_prep_kernel"))) return rc;
   }
-  const size_t smem = 5 * bwd::kTileBytes + bwd::kDqStageBytes + sizeof(BwdSmem);
+  const size_t smem = (3 + 2 * bwd::kStages) * bwd::kTileBytes + sizeof(BwdSmem);
   cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid(B * H, (S_kv + bwd::kTile - 1) / bwd::kTile);
-  attn_bwd_kernel<<<grid, bwd::kThreads, smem, st>>>(mq, mk, mv, mdo, mdq, lse, Delta, (__nv_bfloat16*)dk,
+  attn_bwd_kernel<<<grid, bwd::kThreads, smem, st>>>(mq, mk, mv, mdo, lse, Delta, dQacc, (__nv_bfloat16*)dk,
                                                     (__nv_bfloat16*)dv, S_q, S_kv, q_off,
                                                     scale * 1.4426950408889634f, scale);
   if ((rc = check_launch("attn_bwd_kernel"))) return rc;

@@ -328,14 +328,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 }
 
 // (BH, rows, 128) bf16 tensor viewed as 3-D {128, rows, BH}; boxes of
-// 64 columns x 128 rows with the 128-byte swizzle.
-int make_tmap_rows(CUtensorMap* m, const void* ptr, int rows, int BH) {
+// 64 columns x box_rows rows with the 128-byte swizzle.
+int make_tmap_rows(CUtensorMap* m, const void* ptr, int rows, int BH, int box_rows) {
   auto enc = get_encode_fn();
   if (!enc) { set_error("cuTensorMapEncodeTiled unavailable"); return LH_ERR_LAUNCH; }
   if ((uintptr_t)ptr & 15) { set_error("attention operands must be 16-byte aligned"); return LH_ERR_ARG; }
   cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)BH};
   cuuint64_t strides[2] = {128 * 2, (cuuint64_t)rows * 128 * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -365,9 +365,9 @@ int attn_fwd(const void* q, const void* k, const void* v, int B, int H, int S_q,
              float scale, void* o, float* lse, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
   int rc;
-  if ((rc = make_tmap_rows(&mq, q, S_q, B * H))) return rc;
-  if ((rc = make_tmap_rows(&mk, k, S_kv, B * H))) return rc;
-  if ((rc = make_tmap_rows(&mv, v, S_kv, B * H))) return rc;
+  if ((rc = make_tmap_rows(&mq, q, S_q, B * H, 128))) return rc;
+  if ((rc = make_tmap_rows(&mk, k, S_kv, B * H, 128))) return rc;
+  if ((rc = make_tmap_rows(&mv, v, S_kv, B * H, 128))) return rc;
   const int n_qt = (S_q + fwd::kTile - 1) / fwd::kTile;
   const int n_pairs = (n_qt + 1) / 2;
   const size_t smem = 1024 + fwd::kTileBytes * (2 + 2 * fwd::kNst) + sizeof(FwdSmem);

@@ -62,9 +62,11 @@ struct BwdSmem {
   uint64_t s_ready[2], p_ready[2];                               // per 64-query half
   uint32_t tmem_base;
   int abort;
-  float lse2[2][bwd::kTile];
-  float delta[2][bwd::kTile];
+  __align__(16) float lse2[2][bwd::kTile];     // read as float4
+  __align__(16) float delta[2][bwd::kTile];
 };
+static_assert(offsetof(BwdSmem, lse2) % 16 == 0 && offsetof(BwdSmem, delta) % 16 == 0, "float4 reads");
+static_assert((3 + 2 * bwd::kStages) * bwd::kTileBytes + sizeof(BwdSmem) <= 232448, "shared memory per CTA");
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");

@@ -85,6 +85,103 @@ scatter_fwd_kernel(const T* __restrict__ attn, const int32_t* __restrict__ inver
   }
 }
 
+// ---------------------------------------------------------------- grouped row kernels
+// Scatter forward and un-pool backward over groups of kGroup consecutive
+// tokens: one warp per (32 >> CS neighbouring b*h rows, kGroup tokens), one
+// token of all the warp's heads per step, lanes = head x 16-byte chunk.
+// Per token the output is
+//     out(t) = v_0(t) + base(t),   base(t) = sum_{l >= 1} v_l(t)
+// where v_l(t) is the (scaled) level-l row of the item containing t.  The
+// level-l item changes only every p^l tokens, so base is rebuilt only at those
+// steps; the level-0 row exists for a small fraction of tokens (those selected
+// at full resolution).  The group's inverse-map entries are fetched once per
+// level with coalesced loads and handed out by shuffles.
+//   SHIFTED (scatter, reference :428-458): item jj_l(t) = (t+1)/p^l - 1, rows summed
+//   !SHIFTED (un-pool backward of the mean pooling): jj_l(t) = t/p^l, rows scaled by 1/p^l
+constexpr int kGroup = 16;
+template <class T> struct TypeTag { using type = T; };
+
+template <class T, int LV, int CS, bool SHIFTED>
+__global__ void __launch_bounds__(kRowThreads)
+grouped_rows_kernel(const T* __restrict__ s0, const T* __restrict__ s1, const T* __restrict__ s2,
+                    T* __restrict__ o0, T* __restrict__ o1, T* __restrict__ o2,
+                    const int32_t* __restrict__ inverse, Pyramid pyr, int p_shift, int D, int S_sel,
+                    int N_out, int n_groups, int BH, int H, long long row_stride, long long bh_stride_b,
+                    long long bh_stride_h) {
+  constexpr int VEC = Vec16<T>::N;
+  constexpr int LPH = 1 << CS;                  // lanes per head (16-byte chunks per row)
+  constexpr int HPW = 32 / LPH;                 // heads per warp
+  static_assert(LPH >= kGroup, "one level-0 entry per lane of a head");
+  const T* src0 = blockIdx.y == 0 ? s0 : (blockIdx.y == 1 ? s1 : s2);
+  T* dst0 = blockIdx.y == 0 ? o0 : (blockIdx.y == 1 ? o1 : o2);
+  if (dst0 == nullptr) return;
+  const int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  const int n_hg = BH / HPW;
+  const int grp = w / n_hg;                     // head groups fastest: neighbouring warps, neighbouring rows
+  if (grp >= n_groups) return;
+  const int hh = lane / LPH, jl = lane % LPH;
+  const int bh = (w - grp * n_hg) * HPW + hh;
+  const int b = bh / H, h = bh - b * H;
+  const int tg = grp * kGroup;
+  const int c = jl * VEC;
+  const int32_t* inv = inverse + (size_t)bh * pyr.total;
+  const T* src = src0 + (size_t)bh * S_sel * D + c;
+  T* dst = dst0 + b * bh_stride_b + h * bh_stride_h + c;
+
+  // level-l entries of this group: item first_l + jl for jl < count_l
+  int ent[LV];
+#pragma unroll
+  for (int l = 0; l < LV; ++l) {
+    const int sh = l * p_shift;
+    const int first = SHIFTED ? ((tg + 1) >> sh) - 1 : (tg >> sh);
+    const int last = SHIFTED ? ((tg + kGroup) >> sh) - 1 : ((tg + kGroup - 1) >> sh);
+    const int jj = first + jl;
+    ent[l] = (jj <= last && jj >= 0 && jj < pyr.len[l]) ? __ldg(inv + pyr.off[l] + jj) : -1;
+  }
+  float base[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) base[e] = 0.f;
+#pragma unroll
+  for (int s = 0; s < kGroup; ++s) {
+    const int t = tg + s;
+    if (t >= N_out) break;
+    // rebuild base where any level >= 1 starts a new item (warp-uniform)
+    bool rebuild = s == 0;
+#pragma unroll
+    for (int l = 1; l < LV; ++l) rebuild |= (((SHIFTED ? t + 1 : t) & ((1 << (l * p_shift)) - 1)) == 0);
+    if (rebuild) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) base[e] = 0.f;
+#pragma unroll
+      for (int l = 1; l < LV; ++l) {
+        const int sh = l * p_shift;
+        const int first = SHIFTED ? ((tg + 1) >> sh) - 1 : (tg >> sh);
+        const int idx = (SHIFTED ? ((t + 1) >> sh) - 1 : (t >> sh)) - first;
+        const int slot = __shfl_sync(0xffffffffu, ent[l], hh * LPH + idx);
+        if (slot >= 0) {
+          float v[VEC];
+          load16(src + (size_t)slot * D, v);
+          const float sc = SHIFTED ? 1.0f : 1.0f / (float)(1 << sh);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) base[e] = fmaf(v[e], sc, base[e]);
+        }
+      }
+    }
+    const int slot0 = __shfl_sync(0xffffffffu, ent[0], hh * LPH + s);
+    float acc[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[e] = base[e];
+    if (slot0 >= 0) {
+      float v[VEC];
+      load16(src + (size_t)slot0 * D, v);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] += v[e];
+    }
+    store16(dst + (size_t)t * row_stride, acc);
+  }
+}
+
 // ---------------------------------------------------------------- scatter adjoint
 // dattn[bh, s] = sum over the item's window of dout[bh, pos] (reference :462-514)
 template <class T>
@@ -206,6 +303,39 @@ static bool dispatch_levels(int L, F&& f) {
   return false;
 }
 
+// Launches grouped_rows_kernel when the geometry fits (16 or 32 chunks per
+// row, heads divisible into warps); returns false otherwise.
+template <bool SHIFTED>
+static bool launch_grouped_rows(int dtype, int L, int cs, const void* s0, const void* s1, const void* s2, void* o0,
+                                void* o1, void* o2, int n_tensors, const int32_t* inverse, const Pyramid& pyr,
+                                int p_shift, int D, int S_sel, int N_out, int B, int H, long long row_stride,
+                                long long bh_stride_b, long long bh_stride_h, cudaStream_t st) {
+  if (cs != 4 && cs != 5) return false;
+  const int hpw = 32 >> cs;
+  if ((B * H) % hpw || (SHIFTED ? false : H % hpw)) return false;
+  if (L < 1 || L > 7) return false;
+  const int n_groups = (N_out + kGroup - 1) / kGroup;
+  const long long threads = (long long)(B * H / hpw) * n_groups * 32;
+  dim3 grid((unsigned)((threads + kRowThreads - 1) / kRowThreads), n_tensors);
+  auto go = [&](auto lv) {
+    constexpr int LV = decltype(lv)::value;
+    auto run = [&](auto cs_c, auto t_tag) {
+      constexpr int CS = decltype(cs_c)::value;
+      using T = typename decltype(t_tag)::type;
+      grouped_rows_kernel<T, LV, CS, SHIFTED><<<grid, kRowThreads, 0, st>>>(
+          (const T*)s0, (const T*)s1, (const T*)s2, (T*)o0, (T*)o1, (T*)o2, inverse, pyr, p_shift, D, S_sel, N_out,
+          n_groups, B * H, H, row_stride, bh_stride_b, bh_stride_h);
+    };
+    auto by_cs = [&](auto t_tag) {
+      if (cs == 4) run(std::integral_constant<int, 4>{}, t_tag);
+      else run(std::integral_constant<int, 5>{}, t_tag);
+    };
+    if (dtype == LH_DTYPE_BF16) by_cs(TypeTag<__nv_bfloat16>{});
+    else by_cs(TypeTag<float>{});
+  };
+  return dispatch_levels(L, go);
+}
+
 static int log2i(int x) { int s = 0; while ((1 << s) < x) ++s; return s; }
 
 // chunks of 16 bytes per row as a shift; rejects totals beyond 31 bits
@@ -249,6 +379,10 @@ int scatter_fwd(const void* attn, const int32_t* inverse, int dtype, int B, int 
   int cs; uint32_t n;
   int rc = row_geometry("scatter_fwd", dtype, D, (long long)B * H * N_total, &cs, &n);
   if (rc) return rc;
+  if (launch_grouped_rows<true>(dtype, L, cs, attn, nullptr, nullptr, out, nullptr, nullptr, 1, inverse, pyr,
+                                log2i(p), D, S_sel, N_total, B, H, D, (long long)H * N_total * D,
+                                (long long)N_total * D, st))
+    return check_launch("scatter_fwd (grouped)");
   FastDiv fn(N_total);
   auto go = [&](auto lv) {
     constexpr int LV = decltype(lv)::value;
@@ -258,7 +392,7 @@ int scatter_fwd(const void* attn, const int32_t* inverse, int dtype, int B, int 
       scatter_fwd_kernel<float, LV><<<grid_for(n), kRowThreads, 0, st>>>((const float*)attn, inverse, pyr, log2i(p), D, S_sel, fn, (float*)out, cs, n);
   };
   if (!dispatch_levels(L, go)) { set_error("scatter_fwd: L must be in [1, 7]"); return LH_ERR_SHAPE; }
-  return check_launch("scatter_fwd_kernel");
+  return check_launch("scatter_fwd");
 }
 
 int scatter_bwd(const void* dout, const int32_t* indices, int dtype, int B, int H, int S_sel, int D,
@@ -292,6 +426,9 @@ int unpool_bwd(const void* dq, const void* dk, const void* dv, const int32_t* in
   int cs; uint32_t n;
   int rc = row_geometry("unpool_bwd", dtype, D, (long long)B * S * H, &cs, &n);
   if (rc) return rc;
+  if (launch_grouped_rows<false>(dtype, L, cs, dq, dk, dv, dxq, dxk, dxv, 3, inverse, pyr, log2i(p), D, S_sel, S,
+                                 B, H, (long long)H * D, (long long)S * H * D, D, st))
+    return check_launch("unpool_bwd (grouped)");
   dim3 grid(grid_for(n), 3);
   FastDiv fh(H), fs(S);
   auto go = [&](auto lv) {
@@ -305,7 +442,7 @@ int unpool_bwd(const void* dq, const void* dk, const void* dv, const int32_t* in
     }
   };
   if (!dispatch_levels(L, go)) { set_error("unpool_bwd: L must be in [1, 7]"); return LH_ERR_SHAPE; }
-  return check_launch("unpool_bwd_kernel");
+  return check_launch("unpool_bwd");
 }
 
 }  // namespace lh

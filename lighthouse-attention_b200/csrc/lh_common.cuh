@@ -96,6 +96,18 @@ __device__ __forceinline__ void load16(const float* p, float* f) {
   float4 u = __ldg(reinterpret_cast<const float4*>(p));
   f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
 }
+// 16 raw bytes as VEC floats (the pointer argument only selects the element type).
+__device__ __forceinline__ void unpack16(const uint4& u, float* f, const __nv_bfloat16*) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x; f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ void unpack16(const uint4& u, float* f, const float*) {
+  f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y); f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+}
 __device__ __forceinline__ void store16(__nv_bfloat16* p, const float* f) {
   uint4 u;
   __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);

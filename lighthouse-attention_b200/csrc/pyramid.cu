@@ -15,6 +15,7 @@
 // staged in shared memory and written as contiguous per-head runs.
 #include "lh_common.cuh"
 
+
 namespace lh {
 
 constexpr int kPyrThreads = 128;
@@ -22,7 +23,8 @@ constexpr int kPyrThreads = 128;
 // blockIdx.z selects the tensor (0 = q, 1 = k, 2 = v): each thread carries the
 // level accumulators of one tensor only, and q / k threads also produce that
 // tensor's norm scores.  Loads are double-buffered: the next U tokens are in
-// flight while the current ones are reduced.
+// flight (as raw 16-byte chunks, converted when used) while the current ones
+// are reduced.
 template <class T, int D, int LV>
 __global__ void __launch_bounds__(kPyrThreads)
 pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T* __restrict__ xv,
@@ -31,7 +33,7 @@ pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T
                      float* __restrict__ sqk, float* __restrict__ skq, Pyramid pyr, int S_pool) {
   constexpr int VEC = Vec16<T>::N;       // elements per 16-byte chunk
   constexpr int LPH = D / VEC;           // lanes per head row
-  constexpr int U = 4;                   // tokens per load batch
+  constexpr int U = 4;                   // tokens per load batch (8 needs ~200 registers and is slower)
   static_assert(LPH <= 32 && (32 % LPH) == 0, "head row must fit a warp segment");
   extern __shared__ float s_scores[];    // [H][tpc_tot]
   const int which = blockIdx.z;
@@ -63,18 +65,19 @@ pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T
 #pragma unroll
       for (int e = 0; e < VEC; ++e) acc[l][e] = 0.f;
     }
-    float buf[2][U][VEC];
+    // raw 16-byte chunks in flight (4 registers each); converted when used
+    uint4 raw[2][U];
     auto load_batch = [&](int slot, int i0) {
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        if (active && i0 + u < ntok) load16(src + (size_t)(i0 + u) * tok_stride, buf[slot][u]);
-        else {
-#pragma unroll
-          for (int e = 0; e < VEC; ++e) buf[slot][u][e] = 0.f;
-        }
-      }
+      for (int u = 0; u < U; ++u)
+        raw[slot][u] = (active && i0 + u < ntok)
+                           ? __ldg(reinterpret_cast<const uint4*>(src + (size_t)(i0 + u) * tok_stride))
+                           : make_uint4(0u, 0u, 0u, 0u);
     };
     auto process = [&](int slot, int i0) {
+      float buf[U][VEC];
+#pragma unroll
+      for (int u = 0; u < U; ++u) unpack16(raw[slot][u], buf[u], (const T*)nullptr);
       // the U tokens' norm reductions run side by side (independent shuffle chains)
       float nrms[U];
       if (scored) {
@@ -83,7 +86,7 @@ pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T
         for (int u = 0; u < U; ++u) {
           ss[u] = 0.f;
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) ss[u] = fmaf(buf[slot][u][e], buf[slot][u][e], ss[u]);
+          for (int e = 0; e < VEC; ++e) ss[u] = fmaf(buf[u][e], buf[u][e], ss[u]);
         }
 #pragma unroll
         for (int m = LPH / 2; m > 0; m >>= 1) {
@@ -102,7 +105,7 @@ pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T
 #pragma unroll
         for (int l = 1; l < LV; ++l) {
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) acc[l][e] += buf[slot][u][e];
+          for (int e = 0; e < VEC; ++e) acc[l][e] += buf[u][e];
           mx[l] = fmaxf(mx[l], nrm);
           const int sh = l * p_shift;
           if (((i + 1) & ((1 << sh) - 1)) == 0) {

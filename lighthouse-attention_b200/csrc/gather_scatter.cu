@@ -207,7 +207,18 @@ scatter_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ indic
         const int first = (idx - lvl_off) * f + f - 1;
         const int last = min(first + f, N_total);
         const T* src = dout + (size_t)bh * N_total * D + c;
-        for (int pos = first; pos < last; ++pos) {
+        // four independent loads in flight per trip; the fp32 sum keeps position order
+        int pos = first;
+        for (; pos + 4 <= last; pos += 4) {
+          float v[4][VEC];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) load16(src + (size_t)(pos + u) * D, v[u]);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) acc[e] += v[u][e];
+        }
+        for (; pos < last; ++pos) {
           float v[VEC];
           load16(src + (size_t)pos * D, v);
 #pragma unroll

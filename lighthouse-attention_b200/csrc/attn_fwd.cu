@@ -6,8 +6,8 @@
 // One CTA per (pair of 128-row query tiles A and B, b*h), 384 threads,
 // warp-specialised (warpgroup 0 gives registers to the softmax warpgroups
 // with setmaxnreg: 56 + 2 x 224 per thread-slot = the 3 x 168 of the launch):
-//   warp 0      TMA producer: Q_A and Q_B once, then K/V tiles through a
-//               two-stage ring shared by both query tiles
+//   warp 0      TMA producer: Q_A and Q_B once, then K and V tiles through
+//               two-stage rings shared by both query tiles (K one tile ahead)
 //   warp 1      TMEM owner + MMA issuer (one elected lane):
 //                 S_X = Q_X K_j^T  -> TMEM S_X   (SS MMA, both K-major, SW128)
 //                 O_X += P_X V_j   -> TMEM O_X   (TS MMA: P read from TMEM,
@@ -50,7 +50,7 @@ __device__ int g_attn_status;    // set to 1 when a bounded wait gave up
 
 struct FwdSmem {
   uint64_t q_full;
-  uint64_t k_full[fwd::kNst], v_full[fwd::kNst], kv_empty[fwd::kNst];
+  uint64_t k0_full, kv_full[fwd::kNst], k_empty[fwd::kNst], v_empty[fwd::kNst];   // kv_full[j%2]: K_{j+1} and V_j
   uint64_t s_full[2], p_ready[2], o_final[2];
   uint32_t tmem_base;
   int abort;
@@ -87,7 +87,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   if (threadIdx.x == 0) {
     mbar_init(&sm->q_full, 1);
-    for (int s = 0; s < kNst; ++s) { mbar_init(&sm->k_full[s], 1); mbar_init(&sm->v_full[s], 1); mbar_init(&sm->kv_empty[s], 1); }
+    for (int s = 0; s < kNst; ++s) { mbar_init(&sm->kv_full[s], 1); mbar_init(&sm->k_empty[s], 1); mbar_init(&sm->v_empty[s], 1); }
+    mbar_init(&sm->k0_full, 1);
     for (int x = 0; x < 2; ++x) { mbar_init(&sm->s_full[x], 1); mbar_init(&sm->p_ready[x], 128); mbar_init(&sm->o_final[x], 1); }
     sm->abort = 0;
     fence_mbar_init();
@@ -115,19 +116,35 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         tma_load_3d(sQ + kTileBytes + kBox, &tmQ, &sm->q_full, 64, qt[1] * kTile, bh);
       }
     }
-    for (int j = 0; j < nkv_max; ++j) {
+    // K runs one tile ahead of V: K_j is free once S(j) of both query tiles is
+    // done (one step before V_j, which PV(j) reads), so its refill starts a
+    // step earlier.  K_{j+1} and V_j share one barrier: the MMA warp waits once
+    // per step for both (every wait of the issuing thread idles the pipe).
+    auto load_k = [&](int j, uint64_t* bar) -> bool {
       const int st = j % kNst, round = j / kNst;
-      if (round > 0) {
-        bool ok = mbar_wait(&sm->kv_empty[st], (round - 1) & 1, abort);
-        if (__any_sync(0xffffffffu, !ok)) break;
-      }
+      if (round > 0 && !mbar_wait(&sm->k_empty[st], (round - 1) & 1, abort)) return false;
       if (lane == 0) {
-        mbar_expect_tx(&sm->k_full[st], kTileBytes);
-        tma_load_3d(sK + st * kTileBytes, &tmK, &sm->k_full[st], 0, j * kTile, bh);
-        tma_load_3d(sK + st * kTileBytes + kBox, &tmK, &sm->k_full[st], 64, j * kTile, bh);
-        mbar_expect_tx(&sm->v_full[st], kTileBytes);
-        tma_load_3d(sV + st * kTileBytes, &tmV, &sm->v_full[st], 0, j * kTile, bh);
-        tma_load_3d(sV + st * kTileBytes + kBox, &tmV, &sm->v_full[st], 64, j * kTile, bh);
+        tma_load_3d(sK + st * kTileBytes, &tmK, bar, 0, j * kTile, bh);
+        tma_load_3d(sK + st * kTileBytes + kBox, &tmK, bar, 64, j * kTile, bh);
+      }
+      return true;
+    };
+    bool ok = true;
+    if (nkv_max > 0) {
+      if (lane == 0) mbar_expect_tx(&sm->k0_full, kTileBytes);
+      ok = load_k(0, &sm->k0_full);
+    }
+    for (int j = 0; j < nkv_max && ok; ++j) {
+      const int st = j % kNst, round = j / kNst;
+      const bool next_k = j + 1 < nkv_max;
+      if (round > 0) ok = mbar_wait(&sm->v_empty[st], (round - 1) & 1, abort);
+      if (__any_sync(0xffffffffu, !ok)) break;
+      if (lane == 0) mbar_expect_tx(&sm->kv_full[st], (next_k ? 2 : 1) * kTileBytes);
+      if (next_k) ok = load_k(j + 1, &sm->kv_full[st]);
+      if (__any_sync(0xffffffffu, !ok)) break;
+      if (lane == 0) {
+        tma_load_3d(sV + st * kTileBytes, &tmV, &sm->kv_full[st], 0, j * kTile, bh);
+        tma_load_3d(sV + st * kTileBytes + kBox, &tmV, &sm->kv_full[st], 64, j * kTile, bh);
       }
       __syncwarp();
     }
@@ -156,24 +173,24 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
       if (j == nkv_x - 1) mma_commit(&sm->o_final[x]);
     };
-    bool ok = mbar_wait(&sm->q_full, 0, abort) && mbar_wait(&sm->k_full[0], 0, abort);
+    bool ok = mbar_wait(&sm->q_full, 0, abort) && mbar_wait(&sm->k0_full, 0, abort);
     if (!__any_sync(0xffffffffu, !ok)) {
       tc_fence_after();
       if (lane == 0) {
         issue_s(0, 0);
         if (nkv[1] > 0) issue_s(1, 0);
+        mma_commit(&sm->k_empty[0]);              // K_0 no longer read once these complete
       }
       __syncwarp();
       for (int j = 0; j < nkv_max && ok; ++j) {
         const int st = j % kNst;
-        ok = mbar_wait(&sm->v_full[st], (j / kNst) & 1, abort);
+        ok = mbar_wait(&sm->kv_full[st], (j / kNst) & 1, abort);   // V_j and K_{j+1}
         if (__any_sync(0xffffffffu, !ok)) break;
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           const int nkv_x = x ? nkv[1] : nkv[0];
           if (j >= nkv_x) continue;
           ok = mbar_wait(&sm->p_ready[x], j & 1, abort);
-          if (j + 1 < nkv_x) ok = ok && mbar_wait(&sm->k_full[(j + 1) % kNst], ((j + 1) / kNst) & 1, abort);
           if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
           tc_fence_after();
           if (lane == 0) {
@@ -183,7 +200,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           __syncwarp();
         }
         if (!ok) break;
-        if (lane == 0) mma_commit(&sm->kv_empty[st]);
+        if (lane == 0) {
+          mma_commit(&sm->v_empty[st]);                           // V_j read by PV(j) of both tiles
+          if (j + 1 < nkv_max) mma_commit(&sm->k_empty[(j + 1) % kNst]);   // K_{j+1} read by S(j+1)
+        }
         __syncwarp();
       }
     }

@@ -89,7 +89,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     mbar_init(&sm->q_full, 1);
     for (int s = 0; s < kNst; ++s) { mbar_init(&sm->kv_full[s], 1); mbar_init(&sm->k_empty[s], 1); mbar_init(&sm->v_empty[s], 1); }
     mbar_init(&sm->k0_full, 1);
-    for (int x = 0; x < 2; ++x) { mbar_init(&sm->s_full[x], 1); mbar_init(&sm->p_ready[x], 128); mbar_init(&sm->o_final[x], 1); }
+    for (int x = 0; x < 2; ++x) { mbar_init(&sm->s_full[x], 1); mbar_init(&sm->p_ready[x], 129); mbar_init(&sm->o_final[x], 1); }
     sm->abort = 0;
     fence_mbar_init();
   }
@@ -148,6 +148,25 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       }
       __syncwarp();
     }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ K/V gate
+    // Folds "V_j and K_{j+1} have landed" into p_ready of every tile active at
+    // step j (129 = 128 softmax threads + this warp), so the MMA warp waits
+    // only on p_ready: each wait of the issuing thread idles the tensor pipe.
+    // A phase of p_ready gets this warp's arrival only after the previous one
+    // has completed, so an early arrival never counts toward the wrong step.
+    bool ok = true;
+    for (int j = 0; j < nkv_max && ok; ++j) {
+      ok = mbar_wait(&sm->kv_full[j % kNst], (j / kNst) & 1, abort);
+      if (ok && lane == 0) {
+        if (j < nkv[0]) mbar_arrive(&sm->p_ready[0]);
+        if (j < nkv[1]) mbar_arrive(&sm->p_ready[1]);
+      }
+#pragma unroll
+      for (int x = 0; x < 2; ++x)
+        if (ok && j < (x ? nkv[1] : nkv[0])) ok = mbar_wait(&sm->p_ready[x], j & 1, abort);
+      if (__any_sync(0xffffffffu, !ok)) break;
+    }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc_qk = idesc_bf16_f32(kTile, kTile, false, false);
@@ -184,8 +203,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       __syncwarp();
       for (int j = 0; j < nkv_max && ok; ++j) {
         const int st = j % kNst;
-        ok = mbar_wait(&sm->kv_full[st], (j / kNst) & 1, abort);   // V_j and K_{j+1}
-        if (__any_sync(0xffffffffu, !ok)) break;
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           const int nkv_x = x ? nkv[1] : nkv[0];

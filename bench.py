@@ -164,23 +164,49 @@ def run_ours(args, rank, world, local_rank):
     w = dout  # resident upstream weight: loss = <out, w>
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
 
-    def e2e_step():
-        xs = [t.to(dev, non_blocking=True).requires_grad_(True) for t in (hq, hk, hv)]
-        out = lh.lighthouse_attention(*xs, num_levels=L, pooling_factor=p, topk=k)
-        loss = (out.float() * w.float()).sum()
-        loss.backward()
-        return loss.item()
+    # Input pipeline as in training: step i+1's host->device copy runs on a
+    # second stream while step i computes (two device buffers ordered by
+    # events).  Every step's copy and its loss read-back are inside the timed
+    # region; only their overlap with compute changes.
+    copy_stream = torch.cuda.Stream(device=dev)
+    bufs = [[torch.empty(t.shape, dtype=t.dtype, device=dev) for t in (hq, hk, hv)] for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+    w_f = w.float()  # the resident upstream weight, converted once
 
-    for _ in range(max(1, args.warmup // 2)):
-        e2e_step()
+    def enqueue_copy(slot, after=None):
+        with torch.cuda.stream(copy_stream):
+            if after is not None:
+                copy_stream.wait_event(after)
+            copy_stream.wait_event(freed[slot])      # the step that last read this buffer is done
+            for d_, h_ in zip(bufs[slot], (hq, hk, hv)):
+                d_.copy_(h_, non_blocking=True)
+            copied[slot].record(copy_stream)
+
+    def e2e_run(n, start=None):
+        enqueue_copy(0, start)
+        loss = None
+        for i in range(n):
+            slot = i % 2
+            if i + 1 < n:
+                enqueue_copy((i + 1) % 2)
+            torch.cuda.current_stream().wait_event(copied[slot])
+            xs = [b_.detach().requires_grad_(True) for b_ in bufs[slot]]
+            out = lh.lighthouse_attention(*xs, num_levels=L, pooling_factor=p, topk=k)
+            loss_t = (out * w_f).sum()
+            loss_t.backward()
+            freed[slot].record()
+            loss = loss_t.item()                     # device -> host read of the step's result
+        return loss
+
+    e2e_run(max(2, args.warmup // 2))
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_steps = max(1, min(args.steps, 5))
+    e_steps = max(2, min(args.steps, 5))
     e0.record()
-    for _ in range(e_steps):
-        e2e_step()
+    e2e_run(e_steps, start=e0)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e_steps
@@ -227,7 +253,8 @@ def run_ours(args, rank, world, local_rank):
                     "attn_bwd_ms": bwd_ms, "attn_bwd_tflops": achieved,
                     "rest_ms": ms - fwd_ms - bwd_ms},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms, "api": "lighthouse_attention"},
+                "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms, "api": "lighthouse_attention",
+                "input_pipeline": "step i+1 host->device copy on a second stream during step i"},
         "gpu_launches": 10 * args.steps,
         "clocks": clk.summary(),
     }

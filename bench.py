@@ -259,7 +259,7 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_sample(steps=1, warmup=0)["cpu_baseline"]
+        line["cpu_baseline"] = cpu_sample(steps=2, warmup=1)["cpu_baseline"]   # warm, as the reference arm
     print(json.dumps(line), flush=True)
 
 

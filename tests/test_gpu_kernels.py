@@ -157,3 +157,27 @@ def test_scatter_with_longer_output(lh, O, cuda):
     out = lh._native.scatter_fwd(attn, inv, S, S + 100, L, p)
     ref = O.scatter_to_base(attn, idx.long(), S, S + 100, L, p)
     assert (out - ref).abs().max().item() < 1e-5
+
+
+# Geometries of the grouped scatter / un-pool path (two heads per warp for bf16 D=128):
+# windows wider than the 16-token group (L=3, p=8), many levels (L=5, p=2), and an
+# output longer than the pooled shard.
+@pytest.mark.parametrize("shape", [(1, 8192, 2, 128, 3, 8, 128), (1, 8192, 4, 128, 5, 2, 256),
+                                   (2, 4096, 2, 128, 2, 4, 256)])
+def test_grouped_scatter_and_unpool_vs_oracle(lh, O, cuda, shape):
+    B, S, H, D, L, p, k = shape
+    xq, xk, xv = (t.to(cuda) for t in make_qkv(B, S, H, D, torch.bfloat16, 21))
+    pq, pk, pv, sqk, skq = lh._native.pyramid_score(xq, xk, xv, L, p)
+    idx, inv = lh._native.select_topk(sqk, skq, L, p, k, S)
+    g = torch.Generator().manual_seed(5)
+    attn = torch.randn(B, H, idx.shape[-1], D, generator=g).to(torch.bfloat16).to(cuda)
+    for n_out in (S, S + 37):
+        out = lh._native.scatter_fwd(attn, inv, S, n_out, L, p)
+        ref = O.scatter_to_base(attn.float(), idx.long(), S, n_out, L, p)
+        assert _rel_close(out.float(), ref, BF16_ULP, 1e-6).all()     # the fp32 sum rounded once to bf16
+    dsel = torch.randn(B, H, idx.shape[-1], D, generator=g).to(torch.bfloat16).to(cuda)
+    dxq, _, _ = lh._native.unpool_bwd([dsel, None, None], inv, S, L, p)
+    x = xq.float().clone().requires_grad_(True)
+    _, _, qc, _, _ = O.norm_scorer(x, x, x, p, L)
+    O.gather_rows(qc, idx).backward(dsel.float())
+    assert _rel_close(dxq.float(), x.grad, BF16_ULP, 1e-6).all()

@@ -264,10 +264,13 @@ def run_ours(args, rank, world, local_rank):
 
 
 # ----------------------------------------------------------------------------- model workload
-def run_model(args, rank, world, local_rank):
+def run_model(args, rank, world, local_rank, cp=False):
     """270M Llama3-style training step (Lighthouse on 26 of 30
     layers), bf16 autocast, AdamW, seq 65536, uniform random bytes; DDP over NCCL
-    for N > 1 (weak scaling: every rank trains on its own sequence)."""
+    for N > 1 (weak scaling: every rank trains on its own sequence).  With
+    cp=True (the reference's *_cp flavours) the N ranks
+    train one sequence together: context parallelism over the sequence,
+    gradients averaged by DDP (strong scaling)."""
     import __graft_entry__ as ge
     lh = ge.load_package()
     from lighthouse_b200 import model as M
@@ -278,11 +281,13 @@ def run_model(args, rank, world, local_rank):
     torch.manual_seed(0)
     model = M.Transformer(margs).to(dev)
     model.init_weights(0)
+    if cp and world > 1:
+        model.set_cp_info(rank, world, torch.distributed.new_group(list(range(world))))
     if world > 1:
         model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local_rank], bucket_cap_mb=100,
                                                           gradient_as_bucket_view=True)
     opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
-    g = torch.Generator().manual_seed(1000 + rank)
+    g = torch.Generator().manual_seed(1000 + (0 if cp else rank))   # CP: one sequence shared by all ranks
     host = [torch.randint(0, 256, (1, seq + 1), generator=g, dtype=torch.long).pin_memory() for _ in range(2)]
     toks = [h.to(dev) for h in host]
     for i in range(args.warmup):
@@ -316,15 +321,17 @@ def run_model(args, rank, world, local_rank):
         ms, e2e_ms = t.tolist()
     if rank != 0:
         return
-    tokens = seq * world
+    tokens = seq if cp else seq * world
     n_layers_lh = sum(1 for i in range(margs.n_layers) if i not in margs.lighthouse_full_attn_layers)
     line = {
         "metric": "270M train tok/s (Lighthouse norm, k=2048, p=4, L=3)", "value": tokens / (ms * 1e-3),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 autocast, fp32 master",
+        "higher_is_better": True, "scaling": "strong" if cp else "weak", "vs_baseline": None,
+        "dtype": "bf16 autocast, fp32 master",
         "data": "synthetic (uniform random bytes, seeded)",
         "config": {"workload": "llama3_270m_train_step", "params": M.num_params(model), "seq_len": seq,
-                   "global_batch": world, "lighthouse_layers": n_layers_lh, "parallelism": f"dp{world} (DDP/NCCL)",
+                   "global_batch": 1 if cp else world, "lighthouse_layers": n_layers_lh,
+                   "parallelism": f"cp{world} (LighthouseCP + sharded full attention, NCCL)" if cp else f"dp{world} (DDP/NCCL)",
                    "l2": "activations far larger than L2"},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": (seq + 1) * 8,
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms, "final_loss": loss},
@@ -383,8 +390,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="layer", choices=["layer", "model"],
-                    help="layer: BASELINE config 3 (default); model: config 4, the 270M training step")
+    ap.add_argument("--workload", default="layer", choices=["layer", "model", "model_cp"],
+                    help="layer: BASELINE config 3 (default); model: config 4, the 270M training step; "
+                         "model_cp: config 5, one sequence context-parallel over the N ranks")
     ap.add_argument("--seq-len", type=int, default=None, help="profiling only: override S")
     ap.add_argument("--topk", type=int, default=None, help="profiling only: override k")
     args = ap.parse_args()
@@ -402,8 +410,8 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl")
     try:
-        if args.workload == "model":
-            run_model(args, rank, world, local_rank)
+        if args.workload in ("model", "model_cp"):
+            run_model(args, rank, world, local_rank, cp=args.workload == "model_cp")
         else:
             run_ours(args, rank, world, local_rank)
     finally:

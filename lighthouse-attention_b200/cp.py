@@ -149,3 +149,28 @@ def lighthouse_cp_forward(xq, xk, xv, L: int, p: int, k: int, rank: int, world_s
     out_h = _ScatterInvFn.apply(oh, ih, invh, half, L, p, ops)
     out_t = _ScatterInvFn.apply(ot, it, invt, half, L, p, ops)
     return torch.cat([out_h, out_t], dim=2)
+
+
+def full_cp_attention(xq, xk, xv, rank: int, world_size: int, group, ops=None):
+    """Causal attention over the whole (load-balanced, sharded) sequence: the
+    full-attention layers of a context-parallel model (the reference runs them
+    under torch's context_parallel ring attention, PATCH:754-766).
+    (B, S_local, H, D) x3, local shard = global chunks (rank, 2W-1-rank)
+    -> (B, H, S_local, D).  Same collectives as the Lighthouse layer: one
+    all-gather of K/V, one reduce-scatter of the dK/dV partials."""
+    ops = ops or _native
+    W = max(1, int(world_size))
+    _, s, _, _ = xq.shape
+    half = s // 2
+    t = lambda x, part: x[:, part].transpose(1, 2).contiguous()
+    hp, tp = slice(0, half), slice(half, s)
+    oh, ot = _CPAttentionFn.apply(t(xq, hp), t(xq, tp), t(xk, hp), t(xk, tp), t(xv, hp), t(xv, tp),
+                                  rank, W, group, ops)
+    return torch.cat([oh, ot], dim=2)
+
+
+def shard_sequence(x: torch.Tensor, rank: int, world_size: int, dim: int = 1) -> torch.Tensor:
+    """This rank's load-balanced shard: global chunks rank and 2W-1-rank of 2W."""
+    W = max(1, int(world_size))
+    chunks = x.chunk(2 * W, dim=dim)
+    return torch.cat([chunks[rank], chunks[2 * W - 1 - rank]], dim=dim)

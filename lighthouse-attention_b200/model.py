@@ -11,7 +11,12 @@ architecture in plain PyTorch with the package's Lighthouse layer in the
 attention of every other layer.
 
 Data parallelism is plain DDP over NCCL (gradient all-reduce, bucketed and
-overlapped with backward by torch).
+overlapped with backward by torch).  Context parallelism (the reference's
+`*_cp` flavours, PATCH:325-413, with set_cp_info plumbing PATCH:801-816):
+every rank holds the load-balanced shard (global chunks r and 2W-1-r) of the
+tokens, labels and RoPE positions (PATCH:822-829); Lighthouse layers run
+LighthouseCP and the full-attention layers run causal attention over the
+all-gathered K/V (cp.py); gradients are averaged over ranks by DDP.
 """
 from __future__ import annotations
 
@@ -22,6 +27,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import cp as _cp
 from .lighthouse_selection import lighthouse_attention
 
 
@@ -76,13 +82,19 @@ class Attention(nn.Module):
             raise ValueError("only the `norm` Lighthouse scorer is provided")
         self.L, self.p, self.k = args.lighthouse_num_levels, args.lighthouse_pooling_factor, args.lighthouse_topk
 
-    def forward(self, x, freqs):
+    def forward(self, x, freqs, cp_info=None):
         B, S, _ = x.shape
         xq = self.wq(x).view(B, S, self.n_heads, self.head_dim)
         xk = self.wk(x).view(B, S, self.n_heads, self.head_dim)
         xv = self.wv(x).view(B, S, self.n_heads, self.head_dim)
         xq, xk = apply_rope(xq, freqs), apply_rope(xk, freqs)
-        if self.lighthouse:
+        if cp_info is not None:
+            rank, world, group = cp_info
+            if self.lighthouse:
+                out = _cp.lighthouse_cp_forward(xq, xk, xv, self.L, self.p, self.k, rank, world, group)
+            else:
+                out = _cp.full_cp_attention(xq, xk, xv, rank, world, group)
+        elif self.lighthouse:
             out = lighthouse_attention(xq, xk, xv, self.L, self.p, self.k)          # (B, H, S, D)
         else:
             out = F.scaled_dot_product_attention(xq.transpose(1, 2), xk.transpose(1, 2), xv.transpose(1, 2),
@@ -109,8 +121,8 @@ class Block(nn.Module):
         self.ffn_norm = nn.RMSNorm(args.dim, eps=args.norm_eps)
         self.feed_forward = FeedForward(args.dim, args.hidden_dim)
 
-    def forward(self, x, freqs):
-        h = x + self.attention(self.attention_norm(x), freqs)
+    def forward(self, x, freqs, cp_info=None):
+        h = x + self.attention(self.attention_norm(x), freqs, cp_info)
         return h + self.feed_forward(self.ffn_norm(h))
 
 
@@ -123,6 +135,12 @@ class Transformer(nn.Module):
         self.norm = nn.RMSNorm(args.dim, eps=args.norm_eps)
         self.output = nn.Linear(args.dim, args.vocab_size, bias=False)
         self._freqs = None
+        self.cp_info = None          # (rank, world_size, group) once set_cp_info is called
+
+    def set_cp_info(self, rank: int, world_size: int, group) -> None:
+        """Context-parallel mode (PATCH:801-816): forward then takes this rank's
+        load-balanced token shard and applies RoPE at its global positions."""
+        self.cp_info = (rank, world_size, group) if world_size > 1 else None
 
     def init_weights(self, seed: int = 0):
         g = torch.Generator(device="cpu").manual_seed(seed)
@@ -133,13 +151,17 @@ class Transformer(nn.Module):
 
     def forward(self, tokens):
         B, S = tokens.shape
-        if self._freqs is None or self._freqs.shape[0] < S or self._freqs.device != tokens.device:
-            self._freqs = rope_freqs(self.args.dim // self.args.n_heads, max(S, 1), self.args.rope_theta,
+        W = self.cp_info[1] if self.cp_info else 1
+        S_glob = S * W
+        if self._freqs is None or self._freqs.shape[0] < S_glob or self._freqs.device != tokens.device:
+            self._freqs = rope_freqs(self.args.dim // self.args.n_heads, max(S_glob, 1), self.args.rope_theta,
                                      tokens.device)
-        freqs = self._freqs[:S]
+        freqs = self._freqs[:S_glob]
+        if self.cp_info:
+            freqs = _cp.shard_sequence(freqs, self.cp_info[0], W, dim=0)   # global positions of the shard
         h = self.tok_embeddings(tokens)
         for layer in self.layers:
-            h = layer(h, freqs)
+            h = layer(h, freqs, self.cp_info)
         return self.output(self.norm(h))
 
 
@@ -150,8 +172,16 @@ def num_params(model: nn.Module) -> int:
 def train_step(model, optimizer, tokens: torch.Tensor) -> torch.Tensor:
     """One next-byte-prediction step on tokens (B, S+1): inputs are the first S
     bytes, labels the last S.  bf16 autocast over fp32 master weights (the
-    reference trains with bf16 mixed precision).  Returns the loss tensor."""
+    reference trains with bf16 mixed precision).  In context-parallel mode
+    (model.set_cp_info) every rank passes the same global tokens and trains on
+    its load-balanced shard of inputs and labels; the returned loss is this
+    rank's shard mean.  Returns the loss tensor."""
     inputs, labels = tokens[:, :-1], tokens[:, 1:]
+    core = model.module if hasattr(model, "module") else model
+    if core.cp_info:
+        rank, W, _ = core.cp_info
+        inputs = _cp.shard_sequence(inputs, rank, W, dim=1)
+        labels = _cp.shard_sequence(labels, rank, W, dim=1)
     with torch.autocast("cuda", dtype=torch.bfloat16):
         logits = model(inputs)
     loss = F.cross_entropy(logits.float().reshape(-1, logits.shape[-1]), labels.reshape(-1))

@@ -77,3 +77,49 @@ def test_owner_map():
     W = 4
     owners = [cp._owner(c, W) for c in range(2 * W)]
     assert owners == [(0, 0), (1, 0), (2, 0), (3, 0), (3, 1), (2, 1), (1, 1), (0, 1)]
+
+
+def _full_worker(rank, W, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        sys.path.insert(0, str(ROOT))
+        dist.init_process_group("gloo", rank=rank, world_size=W)
+        import __graft_entry__ as ge
+        from oracle import cp_ops
+        ge.load_package()
+        from lighthouse_b200 import cp
+        S_full, H_, D_ = 2048, 2, 16
+        g = torch.Generator().manual_seed(3)
+        xs = [torch.randn(1, S_full, H_, D_, generator=g) for _ in range(3)]
+        dout = torch.randn(1, H_, S_full, D_, generator=g)
+        local = [cp.shard_sequence(x, rank, W, dim=1).requires_grad_(True) for x in xs]
+        out = cp.full_cp_attention(*local, rank, W, dist.group.WORLD, ops=cp_ops)
+        out.backward(cp.shard_sequence(dout, rank, W, dim=2))
+        xr = [x.clone().requires_grad_(True) for x in xs]
+        ref = torch.nn.functional.scaled_dot_product_attention(*(x.transpose(1, 2) for x in xr), is_causal=True)
+        ref.backward(dout)
+        errs = [(out - cp.shard_sequence(ref, rank, W, dim=2)).abs().max().item()]
+        errs += [(a.grad - cp.shard_sequence(b.grad, rank, W, dim=1)).abs().max().item() for a, b in zip(local, xr)]
+        q.put((rank, errs, None))
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+        q.put((rank, None, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("W", [2, 4])
+def test_full_cp_attention_matches_causal_sdpa(W):
+    """The full-attention layers of the context-parallel model: sharded causal
+    attention over all-gathered K/V equals causal SDPA over the whole sequence."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + W * 7 + os.getpid() % 100
+    procs = [ctx.Process(target=_full_worker, args=(r, W, port, q)) for r in range(W)]
+    for p_ in procs:
+        p_.start()
+    results = [q.get(timeout=600) for _ in range(W)]
+    for p_ in procs:
+        p_.join(timeout=60)
+    for rank, errs, tb in results:
+        assert tb is None, tb
+        assert max(errs) < 1e-4, (rank, errs)

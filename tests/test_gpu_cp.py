@@ -84,3 +84,67 @@ def test_cp_two_gpus_vs_global_semantics():
         assert status == 0
         for m, r in errs:
             assert m <= 2e-2 and r <= 1e-2, (rank, errs)
+
+
+def _model_worker(rank, W, port, q):
+    try:
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        sys.path.insert(0, str(ROOT))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=W, device_id=torch.device("cuda", rank))
+        import __graft_entry__ as ge
+        lh = ge.load_package()
+        from lighthouse_b200 import model as M
+        dev = torch.device("cuda", rank)
+        cp_group = dist.new_group(list(range(W)))          # CP collectives apart from DDP's
+        args = M.ModelArgs(dim=256, n_layers=4, n_heads=2, n_kv_heads=2, hidden_dim=384, max_seq_len=16384,
+                           lighthouse_topk=1024, lighthouse_full_attn_layers=[0])
+        torch.manual_seed(0)
+        m = M.Transformer(args).to(dev)
+        m.init_weights(0)
+        m.set_cp_info(rank, W, cp_group)
+        ddp = torch.nn.parallel.DistributedDataParallel(m, device_ids=[rank])
+        opt = torch.optim.AdamW(ddp.parameters(), lr=3e-3, fused=True)
+        g = torch.Generator().manual_seed(1)
+        base = torch.randint(0, 256, (1, 64), generator=g)
+        tokens = base.repeat(1, 16384 // 64 + 1)[:, :16385].to(dev)   # the same global tokens on every rank
+        losses = []
+        for _ in range(8):
+            loss = M.train_step(ddp, opt, tokens).detach()
+            dist.all_reduce(loss)
+            losses.append(loss.item() / W)
+        flat = torch.cat([p.detach().float().flatten() for p in m.parameters()])
+        lo, hi = flat.clone(), flat.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        spread = (hi - lo).abs().max().item()
+        status = lh._native.device_status()
+        dist.destroy_process_group()
+        q.put((rank, (losses, spread), status, None))
+    except Exception:
+        import traceback
+        q.put((rank, None, None, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_context_parallel_model_trains_on_two_gpus():
+    """Context-parallel training loop: sharded tokens / labels / RoPE positions,
+    LighthouseCP and sharded full attention, DDP gradient averaging."""
+    W = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29800 + os.getpid() % 150
+    procs = [ctx.Process(target=_model_worker, args=(r, W, port, q)) for r in range(W)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=900) for _ in range(W)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, res, status, tb in results:
+        assert tb is None, tb
+        losses, spread = res
+        assert all(torch.isfinite(torch.tensor(losses))), losses
+        assert losses[-1] < losses[0] - 0.5, losses
+        assert spread == 0.0, spread            # replicas stay identical
+        assert status == 0

@@ -168,6 +168,15 @@ int lh_unpool_bwd(const void* dq_sel, const void* dk_sel, const void* dv_sel,
                   const int32_t* inverse, int dtype, int B, int S, int H, int D, int L, int p,
                   int S_sel, void* dxq, void* dxk, void* dxv, void* stream);
 
+/* Rotary position embedding of q and k (model harness; the reference applies
+ * it in torchtitan's attention before the Lighthouse call, PATCH:700-737).
+ *   xq, xk, oq, ok  (B, S, H, D) dtype (oq/ok may alias xq/xk)
+ *   table           (S, D/2, 2) fp32 (cos, sin) per position and pair
+ * Pairs (x[2i], x[2i+1]) rotate by the pair's angle; inverse != 0 rotates by
+ * minus the angle (the backward). */
+int lh_rope_apply(const void* xq, const void* xk, void* oq, void* ok, const float* table, int dtype,
+                  int B, int S, int H, int D, int inverse, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -44,6 +44,7 @@ _SIGS = {
     "lh_scatter_fwd": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
     "lh_scatter_bwd": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
     "lh_unpool_bwd": (ctypes.c_int, [_VP] * 4 + [ctypes.c_int] * 8 + [_VP] * 4),
+    "lh_rope_apply": (ctypes.c_int, [_VP] * 5 + [ctypes.c_int] * 6 + [_VP]),
 }
 
 
@@ -228,3 +229,17 @@ def unpool_bwd(dsels, inverse, S: int, L: int, p: int):
     _check(load().lh_unpool_bwd(*[_ptr(d) for d in dsels], _ptr(inverse), LH_DTYPE[first.dtype], B, S, H, D, L, p,
                                 S_sel, *[_ptr(o) for o in outs], _stream()))
     return outs
+
+
+def rope_apply(xq, xk, table, inverse: bool = False):
+    """Rotary embedding of q and k (B, S, H, D) with the (S, D/2, 2) fp32 (cos, sin)
+    table; returns new tensors.  inverse=True rotates by minus the angles."""
+    xq, xk, table = xq.contiguous(), xk.contiguous(), table.contiguous()
+    B, S, H, D = xq.shape
+    if xk.shape != xq.shape or xk.dtype != xq.dtype or tuple(table.shape) != (S, D // 2, 2):
+        raise LighthouseShapeError("rope: q, k and the table must agree")
+    oq, ok = torch.empty_like(xq), torch.empty_like(xk)
+    _check(load().lh_rope_apply(_ptr(xq), _ptr(xk), _ptr(oq), _ptr(ok), _ptr(table), LH_DTYPE[xq.dtype],
+                                B, S, H, D, int(inverse), _stream()))
+    return oq, ok
+

@@ -61,6 +61,7 @@ int attn_fwd(const void*, const void*, const void*, int, int, int, int, int, int
              cudaStream_t);
 size_t attn_bwd_workspace_size(int, int, int, int, int);
 int attn_status(int reset);
+int rope_apply(const void*, const void*, void*, void*, const float*, int, int, int, int, int, int, cudaStream_t);
 int attn_bwd_noalloc(const void*, const void*, const void*, const void*, const float*, const void*, int, int, int,
                      int, int, int, float, void*, void*, void*, cudaStream_t);
 int attn_bwd(const void*, const void*, const void*, const void*, const float*, const void*, int, int, int, int,
@@ -203,6 +204,18 @@ int lh_unpool_bwd(const void* dq, const void* dk, const void* dv, const int32_t*
   LH_REQUIRE(p >= 2 && (p & (p - 1)) == 0 && L >= 1 && L <= 7, LH_ERR_SHAPE, "unpool_bwd: bad L/p");
   LH_ARCH();
   return unpool_bwd(dq, dk, dv, inverse, dtype, B, S, H, D, L, p, S_sel, dxq, dxk, dxv, S_(stream));
+}
+
+int lh_rope_apply(const void* xq, const void* xk, void* oq, void* ok, const float* table, int dtype, int B, int S,
+                  int H, int D, int inverse, void* stream) {
+  g_err[0] = 0;
+  LH_REQUIRE(xq && xk && oq && ok && table, LH_ERR_ARG, "rope: null pointer");
+  LH_REQUIRE(!(((uintptr_t)xq | (uintptr_t)xk | (uintptr_t)oq | (uintptr_t)ok | (uintptr_t)table) & 15), LH_ERR_ARG,
+             "rope: pointers must be 16-byte aligned");
+  LH_REQUIRE(dtype == LH_DTYPE_BF16 || dtype == LH_DTYPE_F32, LH_ERR_ARG, "rope: bad dtype");
+  LH_REQUIRE(B > 0 && S > 0 && H > 0 && D > 0, LH_ERR_SHAPE, "rope: bad shape");
+  LH_ARCH();
+  return rope_apply(xq, xk, oq, ok, table, dtype, B, S, H, D, inverse, S_(stream));
 }
 
 }  // extern "C"

@@ -27,6 +27,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import _native
 from . import cp as _cp
 from .lighthouse_selection import lighthouse_attention
 
@@ -66,6 +67,29 @@ def apply_rope(x: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
     return out.to(x.dtype)
 
 
+class _RopeFn(torch.autograd.Function):
+    """Fused RoPE of q and k on the GPU (csrc/rope.cu); backward = inverse rotation."""
+
+    @staticmethod
+    def forward(ctx, xq, xk, table):
+        ctx.save_for_backward(table)
+        return _native.rope_apply(xq, xk, table)
+
+    @staticmethod
+    def backward(ctx, gq, gk):
+        (table,) = ctx.saved_tensors
+        dq, dk = _native.rope_apply(gq, gk, table, inverse=True)
+        return dq, dk, None
+
+
+def rope_qk(xq: torch.Tensor, xk: torch.Tensor, freqs: torch.Tensor):
+    """RoPE of q and k: one fused kernel for CUDA tensors, the complex-multiply
+    formulation (apply_rope) on the CPU."""
+    if xq.is_cuda:
+        return _RopeFn.apply(xq, xk, torch.view_as_real(freqs).contiguous())
+    return apply_rope(xq, freqs), apply_rope(xk, freqs)
+
+
 class Attention(nn.Module):
     def __init__(self, args: ModelArgs, layer_id: int):
         super().__init__()
@@ -87,7 +111,7 @@ class Attention(nn.Module):
         xq = self.wq(x).view(B, S, self.n_heads, self.head_dim)
         xk = self.wk(x).view(B, S, self.n_heads, self.head_dim)
         xv = self.wv(x).view(B, S, self.n_heads, self.head_dim)
-        xq, xk = apply_rope(xq, freqs), apply_rope(xk, freqs)
+        xq, xk = rope_qk(xq, xk, freqs)
         if cp_info is not None:
             rank, world, group = cp_info
             if self.lighthouse:

@@ -29,3 +29,23 @@ def test_flavour_is_270m(lh):
         m = M.Transformer(M.ModelArgs())
     n = M.num_params(m)
     assert 2.5e8 < n < 3.0e8, n
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_rope_matches_complex_formulation(lh, cuda, dtype):
+    from lighthouse_b200 import model as M
+    B, S, H, D = 2, 1024, 4, 128
+    g = torch.Generator().manual_seed(3)
+    xq, xk = (torch.randn(B, S, H, D, generator=g).to(dtype).to(cuda).requires_grad_(True) for _ in range(2))
+    freqs = M.rope_freqs(D, S, 1e4, cuda)
+    oq, ok = M.rope_qk(xq, xk, freqs)
+    rq, rk = M.apply_rope(xq, freqs), M.apply_rope(xk, freqs)
+    ulp = 2.0 ** -7 if dtype == torch.bfloat16 else 1e-5
+    for a, b in ((oq, rq), (ok, rk)):
+        assert ((a.float() - b.float()).abs() <= ulp * b.float().abs() + 1e-6).all()
+    gq, gk = (torch.randn(B, S, H, D, generator=g).to(dtype).to(cuda) for _ in range(2))
+    dq, dk = torch.autograd.grad((oq, ok), (xq, xk), (gq, gk))
+    eq, ek = torch.autograd.grad((rq, rk), (xq, xk), (gq, gk))
+    for a, b in ((dq, eq), (dk, ek)):
+        assert ((a.float() - b.float()).abs() <= ulp * b.float().abs() + 1e-5).all()

@@ -49,8 +49,8 @@ constexpr int kD = 128;
 constexpr int kBox = 16384;
 constexpr int kTileBytes = 2 * kBox;
 // warpgroup 0: {TMA producer, MMA issuer, 2 idle}; warpgroup 1: dQ drain;
-// warpgroups 2-3: P / dS (two warps per TMEM lane quadrant)
-constexpr int kThreads = 512;
+// warpgroups 2-5: P / dS (four warps per TMEM lane quadrant, 16 queries of each half)
+constexpr int kThreads = 768;
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384, kTmemCols = 512;
 constexpr int kStages = 2;                 // Q_i / dO_i buffers
 }  // namespace bwd
@@ -126,7 +126,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         mbar_init(&sm->q_empty[s][h], 1);
       }
       mbar_init(&sm->s_ready[h], 1);
-      mbar_init(&sm->p_ready[h], 256);
+      mbar_init(&sm->p_ready[h], 512);
       mbar_init(&sm->dq_free[h], 128);
     }
     sm->abort = 0;
@@ -140,10 +140,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   volatile int* abort = &sm->abort;
 
   if (warp < 4) {
-    // Register split 112 (this warpgroup) + 128 (drain) + 2 x 136 (P / dS) per
-    // thread-slot equals the 4 x 128 of the launch (one aligned setmaxnreg per
-    // warpgroup; .inc may not go below the launch's 128, .dec not above it).
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 112;\n" ::: "memory");
+    // Register split 112 (this warpgroup) + 80 (drain) + 4 x 72 (P / dS) per
+    // thread-slot equals the 6 x 80 of the launch (one aligned setmaxnreg per
+    // warpgroup; .inc may not go below the launch's 80, .dec not above it).
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 112;\n" ::: "memory");
     if (warp == 0) {
       // ---------------------------------------------------------- TMA producer
       if (lane == 0 && n_it > 0) {
@@ -248,8 +248,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         }
       } else {
         // dV += P^T_h dO_h and dK += dS^T_h Q_h with A operands from TMEM:
-        // compute warp w of a quadrant leaves the bf16 pairs of its 32 queries
-        // of half h at columns [64h + 32w, +16) (P^T) and [64h + 32w + 16, +16)
+        // compute warp w of a quadrant leaves the bf16 pairs of its 16 queries
+        // of half h at columns [64h + 16w, +8) (P^T) and [64h + 16w + 8, +8)
         // (dS^T).  dQ_i^T = K^T dS^T goes first after the second half.
         const uint32_t aK = smem_u32(sK), adS = smem_u32(sdS);
         for (int t = 0; t < n_it && ok; ++t) {
@@ -271,10 +271,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
               const uint64_t ddo = mdesc(smem_u32(sdO + st * kTileBytes) + h * 4 * 2048);
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
-                const uint32_t a = tbase + kColS + h * 64 + (kk >> 1) * 32 + (kk & 1) * 8;
+                const uint32_t a = tbase + kColS + h * 64 + kk * 16;   // warp kk's 16 queries: P^T | dS^T
                 const uint32_t acc = (t > 0 || h > 0 || kk > 0) ? 1u : 0u;
                 mma_ts(tbase + kColDV, a, ddo + ((kk * 2048) >> 4), id_kmn, acc);
-                mma_ts(tbase + kColDK, a + 16, dq + ((kk * 2048) >> 4), id_kmn, acc);
+                mma_ts(tbase + kColDK, a + 8, dq + ((kk * 2048) >> 4), id_kmn, acc);
               }
               mma_commit(&sm->q_empty[st][h]);   // Q_h / dO_h of this stage and P^T_h / dS^T_h no longer read
             }
@@ -286,8 +286,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       }
     }
   } else if (warp < 8) {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 128;\n" ::: "memory");
-    // ------------------------------------------------------------ dQ drain
+    // ------------------------------------------------------------ dQ drain (launch registers: 80)
     // TMEM lane = head-dimension column d; each thread adds its d of all 128
     // query rows: a warp's red.global.add covers one 128-byte row segment.
     const int quad = warp & 3;
@@ -325,12 +324,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       }
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 136;\n" ::: "memory");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 72;\n" ::: "memory");
     // ------------------------------------------------------------ P / dS
     const int quad = warp & 3;
     const int r = quad * 32 + lane;                 // key row inside the tile (TMEM lane)
-    const int tid = threadIdx.x - 256;              // 0..255
-    const int g = tid >> 7;                         // which 32 queries of each half
+    const int tid = threadIdx.x - 256;              // 0..511
+    const int g = tid >> 7;                         // which 16 queries of each half
     const int kv_pos = j * kTile + r;
     const uint32_t lane_base = tbase + ((uint32_t)(quad * 32) << 16);
     bool ok = true;
@@ -342,7 +341,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         sm->lse2[buf][tid] = q < S_q ? LSE[(size_t)bh * S_q + q] * 1.4426950408889634f : INFINITY;
         sm->delta[buf][tid] = q < S_q ? Delta[(size_t)bh * S_q + q] : 0.f;
       }
-      named_bar_sync(1, 256);
+      named_bar_sync(1, 512);
       const int q_lo = q_off + i * kTile;
       const bool need_mask = (j * kTile + kTile - 1 > q_lo) || (i * kTile + kTile > S_q) || (j * kTile + kTile > S_kv);
 #pragma unroll 1
@@ -350,13 +349,13 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         ok = mbar_wait(&sm->s_ready[h], t & 1, abort);
         if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
         tc_fence_after();
-        const int qc0 = h * 64 + g * 32;            // this warp's 32 query columns
-        uint32_t s[32], dp[32], pk[16], dsw[16];
-        tmem_ld32(lane_base + kColS + qc0, s);
-        tmem_ld32(lane_base + kColDP + qc0, dp);
+        const int qc0 = h * 64 + g * 16;            // this warp's 16 query columns
+        uint32_t s[16], dp[16], pk[8], dsw[8];
+        tmem_ld16(lane_base + kColS + qc0, s);
+        tmem_ld16(lane_base + kColDP + qc0, dp);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
+        for (int e = 0; e < 16; e += 4) {
           const float4 L4 = *reinterpret_cast<const float4*>(&sm->lse2[buf][qc0 + e]);
           const float4 D4 = *reinterpret_cast<const float4*>(&sm->delta[buf][qc0 + e]);
           const float Ls[4] = {L4.x, L4.y, L4.z, L4.w};
@@ -387,12 +386,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           dsw[e / 2 + 1] = pack_bf16(dr[2], dr[3]);
         }
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
+        for (int v = 0; v < 2; ++v)
           st_sw128(sdS, r, qc0 / 8 + v, make_uint4(dsw[4 * v], dsw[4 * v + 1], dsw[4 * v + 2], dsw[4 * v + 3]));
-        // P^T and dS^T as bf16 pairs into this warp's own 32 S^T columns (no
+        // P^T and dS^T as bf16 pairs into this warp's own 16 S^T columns (no
         // other warp reads them), where the dV / dK MMAs take them as A
-        tmem_st16(lane_base + kColS + qc0, pk);
-        tmem_st16(lane_base + kColS + qc0 + 16, dsw);
+        tmem_st8(lane_base + kColS + qc0, pk);
+        tmem_st8(lane_base + kColS + qc0 + 8, dsw);
         tmem_st_wait();
         fence_async_smem();
         tc_fence_before();
@@ -410,9 +409,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const uint32_t col = which == 0 ? kColDV : kColDK;
         const float mul = which == 0 ? 1.0f : scale;
         __nv_bfloat16* row = (which == 0 ? dV : dK) + ((size_t)bh * S_kv + kv_pos) * kD;
-#pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          const int c = 2 * g + c2;
+        {
+          const int c = g;                          // this warp's 32 columns of dV / dK
           uint32_t v[32];
           if (n_it > 0) {
             tmem_ld32(lane_base + col + c * 32, v);

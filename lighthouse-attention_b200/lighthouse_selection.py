@@ -23,6 +23,7 @@ import math
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import _native
 from .lighthouse_selection_cuda import (LighthouseSelectionQkKqChunkedTopkNvrtc,  # noqa: F401
@@ -85,19 +86,71 @@ class DialatedLighthouseNormScorerCP(DialatedLighthouseNormScorer):
         self._checked = False
 
 
+def _causal_attention(q, k, v):
+    """(B, H, S, D) causal attention: this package's tcgen05 kernel for bf16 with
+    D = 128, scaled_dot_product_attention otherwise."""
+    if q.dtype == torch.bfloat16 and q.shape[-1] == 128 and q.is_cuda:
+        o, _ = _native.attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), 1.0 / math.sqrt(q.shape[-1]))
+        return o
+    return F.scaled_dot_product_attention(q, k, v, is_causal=True)
+
+
 class DilatedLighthouseScorer(nn.Module):
-    """Present so the torchtitan patch imports resolve (SEL:618-689). Only the
-    `norm` scorer is provided by this package."""
+    """Dilated scorer (SEL:618-689): the scores are the norms of attention
+    outputs over dilated views of the sequence (every `dilation`-th token forms
+    one of dilation*H sub-sequences), q attending to k (qk) and k to q (kq);
+    the pyramids are the same level means as the norm scorer's.
+
+    The reference's own wiring of this scorer does not run: the torchtitan
+    patch constructs it with ``head_dim=`` and no ``attention`` (PATCH:623-628
+    vs SEL:619-625), and its forward calls ``view`` on transposed tensors.
+    Here ``attention`` defaults to causal attention (the tcgen05 kernel of this
+    package for bf16 / D = 128), ``head_dim`` is accepted and unused, and the
+    outputs are reshaped back to token order as the reference intends.  The
+    scores only feed the selection (under no_grad in LighthouseLocal, SEL:794),
+    so the scorer attention runs without autograd."""
+
+    def __init__(self, attention=None, dilation: int = 4, pooling_factor: int = 4, levels: int = 3,
+                 head_dim: int | None = None):
+        super().__init__()
+        self.attention = attention if attention is not None else _causal_attention
+        self.dilation = dilation
+        self.pooling_factor = pooling_factor
+        self.levels = levels
+
+    def scores(self, xq, xk, xv):
+        """(scores_qk, scores_kq) over the pyramid, (B, H, S_tot) fp32."""
+        b, s, h, d = xq.shape
+        di = self.dilation
+        if s % di:
+            raise ValueError("dilated scorer: sequence length must be a multiple of the dilation")
+        with torch.no_grad():
+            view = lambda x: x.reshape(b, s // di, di * h, d).transpose(1, 2)     # (b, di*h, s/di, d)
+            back = lambda o: o.transpose(1, 2).reshape(b, s, h, d).contiguous()
+            out_qk = back(self.attention(view(xq), view(xk), view(xv)))
+            out_kq = back(self.attention(view(xk), view(xq), view(xv)))
+            # norms of the outputs, rounded to the dtype, max-pooled per level:
+            # what the pyramid kernel computes for its first two inputs
+            _, _, _, sqk, skq = _native.pyramid_score(out_qk, out_kq, out_kq, self.levels, self.pooling_factor)
+        return sqk, skq
+
+    def forward(self, xq, xk, xv):
+        sqk, skq = self.scores(xq, xk, xv)
+        _, _, xq_cat, xk_cat, xv_cat = _PyramidFn.apply(xq, xk, xv, self.levels, self.pooling_factor)
+        return sqk.to(xq.dtype), skq.to(xq.dtype), xq_cat, xk_cat, xv_cat
+
+
+class DilatedLighthouseGLAScorer(nn.Module):
+    """Present so the torchtitan patch imports resolve (SEL:692-755).  The
+    reference computes its scores with the Triton kernels of the external
+    `fla` package, which this package does not use; LighthouseLocal also never
+    passes the gate it needs (SEL:789 vs PATCH:710)."""
 
     def __init__(self, *args, **kwargs):
         super().__init__()
 
     def forward(self, *args, **kwargs):
-        raise NotImplementedError("lighthouse_b200 provides the `norm` scorer only")
-
-
-class DilatedLighthouseGLAScorer(DilatedLighthouseScorer):
-    """Present so the torchtitan patch imports resolve (SEL:692-755)."""
+        raise NotImplementedError("lighthouse_b200 provides the `norm` and `dilated` scorers")
 
 
 # ----------------------------------------------------------------------------- scatter
@@ -133,10 +186,12 @@ class _LighthouseLayerFn(torch.autograd.Function):
     """One Lighthouse layer (SEL:789-825) as a single autograd node."""
 
     @staticmethod
-    def forward(ctx, xq, xk, xv, L, p, k):
+    def forward(ctx, xq, xk, xv, L, p, k, scores=None):
         B, S, H, D = xq.shape
         xq, xk, xv = xq.contiguous(), xk.contiguous(), xv.contiguous()
         pq, pk, pv, sqk, skq = _native.pyramid_score(xq, xk, xv, L, p)
+        if scores is not None:                  # another scorer's (qk, kq) scores, fp32
+            sqk, skq = (t.to(torch.float32).contiguous() for t in scores)
         idx, inv = _native.select_topk(sqk, skq, L, p, k, S)
         qs, ks, vs = _native.gather_selected([xq, xk, xv], [pq, pk, pv], idx)
         scale = 1.0 / math.sqrt(D)
@@ -154,7 +209,7 @@ class _LighthouseLayerFn(torch.autograd.Function):
         dattn = _native.scatter_bwd(dout, idx, S, S, L, p)
         dqs, dks, dvs = _native.attn_bwd(qs, ks, vs, o, lse, dattn, scale)
         dxq, dxk, dxv = _native.unpool_bwd([dqs, dks, dvs], inv, S, L, p)
-        return dxq, dxk, dxv, None, None, None
+        return dxq, dxk, dxv, None, None, None, None
 
 
 def lighthouse_attention(xq, xk, xv, num_levels: int = 3, pooling_factor: int = 4, topk: int = 1024,
@@ -182,9 +237,15 @@ class LighthouseLocal(nn.Module):
         self.attention = attention
 
     def forward(self, xq, xk, xv):
-        if not isinstance(self.scorer, DialatedLighthouseNormScorer):
-            raise NotImplementedError("lighthouse_b200 implements the `norm` scorer path only")
-        return lighthouse_attention(xq, xk, xv, self.num_levels, self.pooling_factor, self.topk)
+        if isinstance(self.scorer, DialatedLighthouseNormScorer):
+            return lighthouse_attention(xq, xk, xv, self.num_levels, self.pooling_factor, self.topk)
+        if isinstance(self.scorer, DilatedLighthouseScorer):
+            if xq.dtype != torch.bfloat16:
+                raise ValueError("lighthouse_attention computes in bf16")
+            scores = self.scorer.scores(xq, xk, xv)
+            out, _ = _LighthouseLayerFn.apply(xq, xk, xv, self.num_levels, self.pooling_factor, self.topk, scores)
+            return out
+        raise NotImplementedError("lighthouse_b200 provides the `norm` and `dilated` scorers")
 
 
 class LighthouseCP(nn.Module):

@@ -82,3 +82,55 @@ def test_scorer_module_api(lh, O, cuda):
     (a.sum() + 2 * b.sum() + 3 * c.sum()).backward()
     for x, y in zip((xq, xk, xv), xr):
         assert (x.grad.float() - y.grad).abs().max().item() < 1e-2
+
+
+def _ref_dilated_scores(xq, xk, xv, di, L, p):
+    """The reference dilated scorer's scores (SEL:635-689) in plain PyTorch:
+    causal SDPA over the dilated views, bf16 output norms, max over windows."""
+    import torch.nn.functional as F
+    b, s, h, d = xq.shape
+    view = lambda x: x.reshape(b, s // di, di * h, d).transpose(1, 2)
+    back = lambda o: o.transpose(1, 2).reshape(b, s, h, d)
+    outs = [back(F.scaled_dot_product_attention(view(a), view(c), view(xv), is_causal=True))
+            for a, c in ((xq, xk), (xk, xq))]
+    res = []
+    for o in outs:
+        sc = o.norm(dim=-1).transpose(1, 2)                      # (b, h, s) in the input dtype
+        levels = [sc] + [sc[..., : (s // p ** l) * p ** l].reshape(b, h, s // p ** l, p ** l).amax(-1)
+                         for l in range(1, L)]
+        res.append(torch.cat(levels, dim=-1).float())
+    return res
+
+
+@pytest.mark.parametrize("shape", [(1, 8192, 2, 3, 4, 256, 4), (1, 16384, 2, 3, 4, 512, 2)])
+def test_dilated_scorer_and_layer(lh, O, cuda, shape):
+    B, S, H, L, p, k, di = shape
+    D = 128
+    xq, xk, xv = make_qkv(B, S, H, D, torch.bfloat16, 23)
+    scorer = lh.DilatedLighthouseScorer(head_dim=D, dilation=di, pooling_factor=p, levels=L)   # patch signature
+    xs = [t.to(cuda).requires_grad_(True) for t in (xq, xk, xv)]
+    sqk, skq = scorer.scores(*[t.detach() for t in xs])
+    rqk, rkq = _ref_dilated_scores(*[t.detach() for t in xs], di, L, p)
+    for ours, ref in ((sqk, rqk), (skq, rkq)):       # different attention kernels: within two bf16 ulps
+        assert ((ours - ref).abs() <= 2 * 2.0 ** -7 * ref.abs() + 1e-6).all()
+    # the scorer module's outputs have the reference's shapes and pyramids
+    s_qk, s_kq, qc, kc, vc = scorer(*xs)
+    assert s_qk.shape == (B, H, O.pyramid_len(S, L, p)) and qc.shape == (B, H, O.pyramid_len(S, L, p), D)
+    _, _, rqc, _, _ = O.norm_scorer(xq.to(cuda), xk.to(cuda), xv.to(cuda), p, L)
+    assert ((qc.detach().float() - rqc.float()).abs() <= 2.0 ** -7 * rqc.float().abs() + 1e-6).all()
+    # the layer with the dilated scores vs the oracle on the same selection
+    g = torch.Generator().manual_seed(24)
+    dout = torch.randn(B, H, S, D, generator=g).to(torch.bfloat16)
+    layer = lh.LighthouseLocal(None, scorer, num_levels=L, pooling_factor=p, topk=k)
+    out = layer(*xs)
+    out.backward(dout.to(cuda))
+    idx = O.select(sqk.cpu(), skq.cpu(), L, p, k, S)
+    xr = [t.float().requires_grad_(True) for t in (xq, xk, xv)]
+    ref, _ = O.lighthouse_local(*xr, L, p, k, indices=idx)
+    ref.backward(dout.float())
+    m, r = _err(out.cpu(), ref)
+    assert m <= 2e-2 and r <= 1e-2, f"out max-abs {m:.3e} rel {r:.3e}"
+    for a, b, n in zip(xs, xr, "qkv"):
+        m, r = _err(a.grad.cpu(), b.grad)
+        assert m <= 2e-2 and r <= 1e-2, f"d{n} max-abs {m:.3e} rel {r:.3e}"
+    assert lh._native.device_status() == 0

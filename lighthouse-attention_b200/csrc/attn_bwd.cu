@@ -333,7 +333,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     const int kv_pos = j * kTile + r;
     const uint32_t lane_base = tbase + ((uint32_t)(quad * 32) << 16);
     bool ok = true;
-    for (int t = 0; t < n_it && ok; ++t) {
+    // Every compute warp meets the named barrier below once per tile, also
+    // after one of its bounded waits failed (it then skips the tile's work):
+    // a warp leaving the loop early would leave the others waiting at it.
+    for (int t = 0; t < n_it; ++t) {
       const int i = i0 + t;
       const int buf = t & 1;
       if (tid < kTile) {
@@ -342,6 +345,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         sm->delta[buf][tid] = q < S_q ? Delta[(size_t)bh * S_q + q] : 0.f;
       }
       named_bar_sync(1, 512);
+      if (!ok) continue;
       const int q_lo = q_off + i * kTile;
       const bool need_mask = (j * kTile + kTile - 1 > q_lo) || (i * kTile + kTile > S_q) || (j * kTile + kTile > S_kv);
 #pragma unroll 1

@@ -177,6 +177,18 @@ int lh_unpool_bwd(const void* dq_sel, const void* dk_sel, const void* dv_sel,
 int lh_rope_apply(const void* xq, const void* xk, void* oq, void* ok, const float* table, int dtype,
                   int B, int S, int H, int D, int inverse, void* stream);
 
+/* Simple gated linear attention forward, the sequence mixer of the `gla`
+ * scorer: replaces fla.ops.simple_gla.chunk_simple_gla (fla 0.5.1) as called
+ * by DilatedLighthouseGLAScorer.forward (src/lighthouse_selection.py:725-726)
+ * with initial_state = None and output_final_state = False.
+ *   q, k, v, o   (B, T, H, 128) bf16 (fla's head-last layout)
+ *   g            (B, T, H) fp32 log-gate per step
+ *   o_t = scale * sum_{s <= t} exp(G_t - G_s) (q_t . k_s) v_s,  G = cumsum(g)
+ * A second (q2, k2, o2) triple sharing v and g runs in the same launch (the
+ * scorer's q->k and k->q passes); pass NULL for all three to skip it. */
+int lh_simple_gla_fwd(const void* q, const void* k, const void* v, const float* g, void* o, const void* q2,
+                      const void* k2, void* o2, int dtype, int B, int T, int H, int D, float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -45,6 +45,7 @@ _SIGS = {
     "lh_scatter_bwd": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
     "lh_unpool_bwd": (ctypes.c_int, [_VP] * 4 + [ctypes.c_int] * 8 + [_VP] * 4),
     "lh_rope_apply": (ctypes.c_int, [_VP] * 5 + [ctypes.c_int] * 6 + [_VP]),
+    "lh_simple_gla_fwd": (ctypes.c_int, [_VP] * 8 + [ctypes.c_int] * 5 + [ctypes.c_float, _VP]),
 }
 
 
@@ -243,3 +244,24 @@ def rope_apply(xq, xk, table, inverse: bool = False):
                                 B, S, H, D, int(inverse), _stream()))
     return oq, ok
 
+
+
+def simple_gla_fwd(q, k, v, g, scale: float, q2=None, k2=None):
+    """Simple GLA forward (fla's chunk_simple_gla, zero initial state) of (B, T, H, 128)
+    bf16 q/k/v with the (B, T, H) log-gate g; returns o, or (o, o2) when the second
+    pass (q2, k2) sharing v and g is given."""
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    g = g.float().contiguous()
+    B, T, H, D = q.shape
+    if k.shape != q.shape or v.shape != q.shape or tuple(g.shape) != (B, T, H):
+        raise LighthouseShapeError("gla: q, k, v (B, T, H, D) and g (B, T, H) must agree")
+    o = torch.empty_like(q)
+    o2 = None
+    if q2 is not None:
+        q2, k2 = q2.contiguous(), k2.contiguous()
+        if q2.shape != q.shape or k2.shape != q.shape:
+            raise LighthouseShapeError("gla: the second pass must have the shape of the first")
+        o2 = torch.empty_like(q)
+    _check(load().lh_simple_gla_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(o), _ptr(q2), _ptr(k2), _ptr(o2),
+                                    LH_DTYPE[q.dtype], B, T, H, D, scale, _stream()))
+    return o if q2 is None else (o, o2)

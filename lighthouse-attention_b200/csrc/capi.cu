@@ -62,6 +62,8 @@ int attn_fwd(const void*, const void*, const void*, int, int, int, int, int, int
 size_t attn_bwd_workspace_size(int, int, int, int, int);
 int attn_status(int reset);
 int rope_apply(const void*, const void*, void*, void*, const float*, int, int, int, int, int, int, cudaStream_t);
+int simple_gla_fwd(const void*, const void*, void*, const void*, const void*, void*, const void*, const float*, int, int,
+                   int, float, cudaStream_t);
 int attn_bwd_noalloc(const void*, const void*, const void*, const void*, const float*, const void*, int, int, int,
                      int, int, int, float, void*, void*, void*, cudaStream_t);
 int attn_bwd(const void*, const void*, const void*, const void*, const float*, const void*, int, int, int, int,
@@ -216,6 +218,21 @@ int lh_rope_apply(const void* xq, const void* xk, void* oq, void* ok, const floa
   LH_REQUIRE(B > 0 && S > 0 && H > 0 && D > 0, LH_ERR_SHAPE, "rope: bad shape");
   LH_ARCH();
   return rope_apply(xq, xk, oq, ok, table, dtype, B, S, H, D, inverse, S_(stream));
+}
+
+int lh_simple_gla_fwd(const void* q, const void* k, const void* v, const float* g, void* o, const void* q2,
+                      const void* k2, void* o2, int dtype, int B, int T, int H, int D, float scale, void* stream) {
+  g_err[0] = 0;
+  LH_REQUIRE(q && k && v && g && o, LH_ERR_ARG, "gla: null pointer");
+  LH_REQUIRE((q2 == nullptr) == (k2 == nullptr) && (q2 == nullptr) == (o2 == nullptr), LH_ERR_ARG,
+             "gla: q2, k2 and o2 must be given together");
+  LH_REQUIRE(!(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o | (uintptr_t)q2 | (uintptr_t)k2 |
+                (uintptr_t)o2) & 15) && !((uintptr_t)g & 3), LH_ERR_ARG, "gla: pointers must be 16-byte aligned");
+  LH_REQUIRE(dtype == LH_DTYPE_BF16, LH_ERR_ARG, "gla: bf16 only");
+  LH_REQUIRE(D == 128, LH_ERR_SHAPE, "gla: head_dim must be 128");
+  LH_REQUIRE(B > 0 && T > 0 && H > 0 && B <= 32767 && H <= 65535, LH_ERR_SHAPE, "gla: bad shape");
+  LH_ARCH();
+  return simple_gla_fwd(q, k, o, q2, k2, o2, v, g, B, T, H, scale, S_(stream));
 }
 
 }  // extern "C"

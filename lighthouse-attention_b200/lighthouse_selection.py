@@ -141,16 +141,46 @@ class DilatedLighthouseScorer(nn.Module):
 
 
 class DilatedLighthouseGLAScorer(nn.Module):
-    """Present so the torchtitan patch imports resolve (SEL:692-755).  The
-    reference computes its scores with the Triton kernels of the external
-    `fla` package, which this package does not use; LighthouseLocal also never
-    passes the gate it needs (SEL:789 vs PATCH:710)."""
+    """Gated-linear-attention scorer (SEL:692-755): the scores are the norms of
+    simple-GLA outputs over the dilated views (dilation*H sub-sequences of every
+    `dilation`-th token), q->k and k->q sharing v and the per-(token, head)
+    log-gate gk; the pyramids are the norm scorer's level means.
 
-    def __init__(self, *args, **kwargs):
+    The reference takes simple GLA from the external fla package
+    (chunk_simple_gla, SEL:725-726); here both passes run in one launch of this
+    package's kernel (csrc/gla.cu, bf16, head_dim 128), and the norms and level
+    maxima come from the pyramid kernel.  Like the reference, the scores are
+    used for selection only and carry no gradient (the gate gets none either)."""
+
+    def __init__(self, head_dim: int, dilation: int = 4, pooling_factor: int = 4, levels: int = 3):
         super().__init__()
+        self.head_dim = head_dim
+        self.dilation = dilation
+        self.pooling_factor = pooling_factor
+        self.levels = levels
+        self.scaling = 1.0 / math.sqrt(head_dim)
 
-    def forward(self, *args, **kwargs):
-        raise NotImplementedError("lighthouse_b200 provides the `norm` and `dilated` scorers")
+    def scores(self, xq, xk, xv, gk):
+        """(scores_qk, scores_kq) over the pyramid, (B, H, S_tot) fp32."""
+        b, s, h, d = xq.shape
+        di = self.dilation
+        if s % di:
+            raise ValueError("gla scorer: sequence length must be a multiple of the dilation")
+        if gk is None or tuple(gk.shape) != (b, s, h):
+            raise ValueError("gla scorer: needs the gate gk of shape (B, S, H)")
+        with torch.no_grad():
+            view = lambda x: x.reshape(b, s // di, di * h, d)          # fla's (B, T, H, D) layout
+            gd = gk.detach().reshape(b, s // di, di * h)
+            o_qk, o_kq = _native.simple_gla_fwd(view(xq), view(xk), view(xv), gd, self.scaling,
+                                                q2=view(xk), k2=view(xq))
+            o_qk, o_kq = o_qk.view(b, s, h, d), o_kq.view(b, s, h, d)
+            _, _, _, sqk, skq = _native.pyramid_score(o_qk, o_kq, o_kq, self.levels, self.pooling_factor)
+        return sqk, skq
+
+    def forward(self, xq, xk, xv, gk):
+        sqk, skq = self.scores(xq, xk, xv, gk)
+        _, _, xq_cat, xk_cat, xv_cat = _PyramidFn.apply(xq, xk, xv, self.levels, self.pooling_factor)
+        return sqk.to(xq.dtype), skq.to(xq.dtype), xq_cat, xk_cat, xv_cat
 
 
 # ----------------------------------------------------------------------------- scatter
@@ -236,16 +266,21 @@ class LighthouseLocal(nn.Module):
         self.topk = topk
         self.attention = attention
 
-    def forward(self, xq, xk, xv):
+    def forward(self, xq, xk, xv, gk=None):
+        """``gk`` is the GLA scorer's gate (B, S, H); the torchtitan patch passes it
+        by keyword (PATCH:708-710), which the reference's forward does not accept."""
         if isinstance(self.scorer, DialatedLighthouseNormScorer):
             return lighthouse_attention(xq, xk, xv, self.num_levels, self.pooling_factor, self.topk)
-        if isinstance(self.scorer, DilatedLighthouseScorer):
+        if isinstance(self.scorer, (DilatedLighthouseScorer, DilatedLighthouseGLAScorer)):
             if xq.dtype != torch.bfloat16:
                 raise ValueError("lighthouse_attention computes in bf16")
-            scores = self.scorer.scores(xq, xk, xv)
+            if isinstance(self.scorer, DilatedLighthouseGLAScorer):
+                scores = self.scorer.scores(xq, xk, xv, gk)
+            else:
+                scores = self.scorer.scores(xq, xk, xv)
             out, _ = _LighthouseLayerFn.apply(xq, xk, xv, self.num_levels, self.pooling_factor, self.topk, scores)
             return out
-        raise NotImplementedError("lighthouse_b200 provides the `norm` and `dilated` scorers")
+        raise NotImplementedError(f"unsupported scorer {type(self.scorer).__name__}")
 
 
 class LighthouseCP(nn.Module):

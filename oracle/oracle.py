@@ -7,7 +7,8 @@ Parity status: the selection restatement (``lh_oracle.c``) is pinned against
 the reference's own kernel source run on host threads (``oracle/_ref``,
 ``build.py``) and, on the GPU box, compiled with the reference's NVRTC flags.
 The scorer, gathers, SDPA and scatter are restated with the same ATen calls
-the reference makes; golden vectors from the reference's own Python code
+the reference makes; the GLA scorer's sequence mixer (the external fla
+package's simple GLA) is restated as its defining recurrence; golden vectors from the reference's own Python code
 (scorer on CPU, Triton scatter kernels in Triton's interpreter) are committed
 under ``tests/golden/`` with the script that made them.
 
@@ -183,6 +184,50 @@ def norm_scorer(xq, xk, xv, p: int, L: int):
     b, s, h, d = xq.shape
     sqk = xq.norm(dim=-1)
     skq = xk.norm(dim=-1)
+    lq, lk, lv, lsq, lsk = [xq], [xk], [xv], [sqk], [skq]
+    for level in range(1, L):
+        pf = p ** level
+        n = s // pf
+        lq.append(xq[:, : n * pf].view(b, n, pf, h, d).mean(2))
+        lk.append(xk[:, : n * pf].view(b, n, pf, h, d).mean(2))
+        lv.append(xv[:, : n * pf].view(b, n, pf, h, d).mean(2))
+        lsq.append(sqk[:, : n * pf].view(b, n, pf, h).max(2).values)
+        lsk.append(skq[:, : n * pf].view(b, n, pf, h).max(2).values)
+    cat = lambda xs: torch.cat(xs, dim=1).transpose(1, 2)
+    return cat(lsq), cat(lsk), cat(lq), cat(lk), cat(lv)
+
+
+def simple_gla(q, k, v, g, scale: float):
+    """Simple gated linear attention, forward, zero initial state: the function the
+    reference's GLA scorer takes from the external flash-linear-attention package
+    (fla 0.5.1, ``fla.ops.simple_gla.chunk_simple_gla``, called at SEL:725-726).
+    Its published definition, stepped as the recurrence over time
+        S_t = exp(g_t) S_{t-1} + k_t v_t^T,     o_t = scale * q_t S_t
+    in fp32.  q, k, v (B, T, H, D); g (B, T, H); returns o in q's dtype."""
+    dt = q.dtype
+    q, k, v, g = (x.float() for x in (q, k, v, g))
+    B, T, H, D = q.shape
+    state = torch.zeros(B, H, D, v.shape[-1], dtype=torch.float32, device=q.device)
+    out = torch.empty(B, T, H, v.shape[-1], dtype=torch.float32, device=q.device)
+    for t in range(T):
+        state = state * g[:, t].exp()[..., None, None] + k[:, t, :, :, None] * v[:, t, :, None, :]
+        out[:, t] = scale * torch.einsum("bhd,bhde->bhe", q[:, t], state)
+    return out.to(dt)
+
+
+def gla_scorer(xq, xk, xv, gk, dilation: int, p: int, L: int):
+    """DilatedLighthouseGLAScorer.forward (SEL:711-755): simple GLA over the
+    dilated views (b, s/di, di*h, d) in both directions (q->k, k->q) sharing v
+    and the gate, output norms as scores, then the pyramid of the norm scorer
+    (level means of x, level maxima of the scores)."""
+    b, s, h, d = xq.shape
+    di = dilation
+    view = lambda x: x.reshape(b, s // di, di * h, *x.shape[3:])
+    gd = gk.reshape(b, s // di, di * h)
+    scale = 1.0 / math.sqrt(d)
+    o_qk = simple_gla(view(xq), view(xk), view(xv), gd, scale).reshape(b, s, h, d)
+    o_kq = simple_gla(view(xk), view(xq), view(xv), gd, scale).reshape(b, s, h, d)
+    sqk, skq = o_qk.norm(dim=-1), o_kq.norm(dim=-1)
     lq, lk, lv, lsq, lsk = [xq], [xk], [xv], [sqk], [skq]
     for level in range(1, L):
         pf = p ** level

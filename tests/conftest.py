@@ -29,7 +29,7 @@ def O():
 def golden():
     import numpy as np
     d = ROOT / "tests" / "golden"
-    return {n: np.load(d / f"{n}.npz") for n in ("scorer", "select", "scatter", "layer")}
+    return {n: np.load(d / f"{n}.npz") for n in ("scorer", "select", "scatter", "layer", "gla")}
 
 
 @pytest.fixture(scope="session")

@@ -42,6 +42,15 @@ LAYER_CASES = {
     "s4096_L3p4_k256": (1, 4096, 1, 16, 3, 4, 256, 41),
 }
 
+# name: (B, S, H, D, dilation, L, p, dtype, gate divisor, seed); the gate is
+# logsigmoid(N(0,1)) / divisor per (token, head), as PATCH:709 makes it
+GLA_CASES = {
+    "f32_d16_di4": (1, 256, 2, 16, 4, 3, 4, torch.float32, 16.0, 51),
+    "f32_d32_di2": (2, 512, 1, 32, 2, 2, 2, torch.float32, 1.0, 52),
+    "bf16_d128_di4": (1, 2048, 2, 128, 4, 3, 4, torch.bfloat16, 16.0, 53),
+    "bf16_d128_ragged": (1, 1600, 2, 128, 4, 3, 4, torch.bfloat16, 2.0, 54),
+}
+
 
 def pyramid_len(N, L, p):
     return sum(N // p ** l for l in range(L))
@@ -50,6 +59,11 @@ def pyramid_len(N, L, p):
 def make_qkv(B, S, H, D, dtype, seed):
     g = torch.Generator().manual_seed(seed)
     return tuple(torch.randn(B, S, H, D, generator=g).to(dtype) for _ in range(3))
+
+
+def make_gate(B, S, H, div, seed):
+    g = torch.Generator().manual_seed(seed + 1000)
+    return torch.nn.functional.logsigmoid(torch.randn(B, S, H, generator=g)) / div
 
 
 def make_scores(B, H, N, L, p, mode, seed):

@@ -2,7 +2,8 @@
 
 Run in the build container (the reference tree is not on the GPU box):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py          # every fixture
+    python tests/golden/make_golden.py gla      # only gla.npz
 
 What produces each fixture (reference paths inside the reference project):
   scorer.npz     DialatedLighthouseNormScorer.forward (src/lighthouse_selection.py:589-616),
@@ -13,6 +14,11 @@ What produces each fixture (reference paths inside the reference project):
                  stable sort + gather of src/lighthouse_selection_cuda.py:425-427.
   scatter.npz    _ScatterToBaseAutograd forward/backward with the reference Triton
                  kernels (src/lighthouse_selection.py:408-576) in Triton's CPU interpreter.
+  gla.npz        DilatedLighthouseGLAScorer.forward (src/lighthouse_selection.py:711-755),
+                 imported unmodified and run on CPU, with its `chunk_simple_gla` (the
+                 external flash-linear-attention package, fla 0.5.1, whose Triton
+                 kernels need a GPU) replaced by that package's own reference
+                 implementation of the same function, `naive_recurrent_simple_gla`.
   layer.npz      LighthouseLocal's forward (src/lighthouse_selection.py:789-825) composed
                  from the pieces above and CPU SDPA (selection from the reference kernel
                  source on host threads, since the reference asserts CUDA for it).
@@ -37,7 +43,8 @@ ROOT = HERE.parent.parent
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(HERE))
 
-from inputs import SCORER_CASES, SELECT_CASES, SCATTER_CASES, LAYER_CASES, checksum, make_scores, make_qkv  # noqa: E402
+from inputs import (GLA_CASES, SCORER_CASES, SELECT_CASES, SCATTER_CASES, LAYER_CASES, checksum, make_gate,
+                    make_scores, make_qkv)  # noqa: E402
 
 REF = pathlib.Path("/root/reference/src")
 
@@ -61,7 +68,34 @@ def load_reference():
     return _load("torchtitan.models.llama3.model.lighthouse_selection", REF / "lighthouse_selection.py")
 
 
+def make_gla(sel):
+    from fla.ops.simple_gla.naive import naive_recurrent_simple_gla
+
+    def chunk_simple_gla(q, k, v, g, scale=None):
+        o, _ = naive_recurrent_simple_gla(q, k, v, g, scale=scale, output_final_state=False)
+        return o.contiguous(), None          # chunk_simple_gla returns a contiguous (B, T, H, D) tensor
+
+    sel.chunk_simple_gla = chunk_simple_gla
+    out = {}
+    for name, (B, S, H, D, di, L, p, dtype, div, seed) in GLA_CASES.items():
+        xq, xk, xv = make_qkv(B, S, H, D, dtype, seed)
+        gk = make_gate(B, S, H, div, seed)
+        with torch.no_grad():
+            sqk, skq, qc, kc, vc = sel.DilatedLighthouseGLAScorer(D, dilation=di, pooling_factor=p, levels=L)(
+                xq, xk, xv, gk)
+        out[f"{name}/checksum"] = np.array(checksum(xq, xk, xv, gk))
+        out[f"{name}/scores_qk"] = sqk.float().numpy()
+        out[f"{name}/scores_kq"] = skq.float().numpy()
+        if D <= 32:                               # the pooling is the norm scorer's; keep the file small
+            out[f"{name}/pooled_q"] = qc[:, :, S:].float().numpy()
+    np.savez_compressed(HERE / "gla.npz", **out)
+    print("gla", (HERE / "gla.npz").stat().st_size, "bytes")
+
+
 def main():
+    if sys.argv[1:] == ["gla"]:
+        make_gla(load_reference())
+        return
     from oracle import build as ob, oracle as O
     ob.build_oracle()
     ob.build_ref(gpu=False)
@@ -116,6 +150,7 @@ def main():
         out[f"{name}/indices"] = idx.numpy()
         out[f"{name}/out"] = res.numpy()
     np.savez_compressed(HERE / "layer.npz", **out)
+    make_gla(sel)
     for f in ("scorer", "select", "scatter", "layer"):
         print(f, (HERE / f"{f}.npz").stat().st_size, "bytes")
 

@@ -4,8 +4,8 @@ import numpy as np
 import pytest
 import torch
 
-from inputs import (LAYER_CASES, SCATTER_CASES, SCORER_CASES, SELECT_CASES, checksum, make_qkv, make_scores,
-                    pyramid_len)
+from inputs import (GLA_CASES, LAYER_CASES, SCATTER_CASES, SCORER_CASES, SELECT_CASES, checksum, make_gate, make_qkv,
+                    make_scores, pyramid_len)
 
 
 @pytest.mark.parametrize("name", list(SCORER_CASES))
@@ -105,3 +105,39 @@ def test_cp_emulation_with_one_rank_equals_local_on_halves(O):
     out, idxs = O.lighthouse_cp_global(xq, xk, xv, 1, 3, 4, 512)
     assert out.shape == (1, 1, 8192, 16) and len(idxs) == 2
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("name", list(GLA_CASES))
+def test_gla_scorer_matches_reference_golden(O, golden, name):
+    """The GLA scorer restatement vs the reference scorer run on CPU with fla's own
+    reference recurrence as its sequence mixer.  fp32: summation order only;
+    bf16 outputs: the two fp32 recurrences may round an output element to
+    neighbouring bf16 values, so scores agree to one bf16 ulp."""
+    B, S, H, D, di, L, p, dtype, div, seed = GLA_CASES[name]
+    xq, xk, xv = make_qkv(B, S, H, D, dtype, seed)
+    gk = make_gate(B, S, H, div, seed)
+    g = golden["gla"]
+    assert str(g[f"{name}/checksum"]) == checksum(xq, xk, xv, gk), "seeded inputs drifted"
+    sqk, skq, qc, _, _ = O.gla_scorer(xq, xk, xv, gk, di, p, L)
+    for ours, key in ((sqk, "scores_qk"), (skq, "scores_kq")):
+        ref = torch.from_numpy(g[f"{name}/{key}"])
+        tol = 1e-5 * ref.abs() + 1e-6 if dtype == torch.float32 else 2.0 ** -7 * ref.abs() + 1e-6
+        assert ((ours.float() - ref).abs() <= tol).all(), key
+    if f"{name}/pooled_q" in g:
+        assert np.array_equal(qc[:, :, S:].float().numpy(), g[f"{name}/pooled_q"])
+
+
+def test_gla_recurrence_equals_closed_form(O):
+    """The recurrence equals the closed form o_t = scale sum_{s<=t} exp(G_t-G_s)(q_t.k_s) v_s
+    (quadratic) that the chunked kernels evaluate, including ragged T."""
+    g = torch.Generator().manual_seed(7)
+    B, T, H, D = 2, 100, 3, 8
+    q, k, v = (torch.randn(B, T, H, D, generator=g, dtype=torch.float64) for _ in range(3))
+    gate = torch.nn.functional.logsigmoid(torch.randn(B, T, H, generator=g, dtype=torch.float64))
+    o = O.simple_gla(q, k, v, gate, 0.3).double()
+    G = gate.cumsum(1)                                                       # (B, T, H)
+    dec = (G[:, :, None, :] - G[:, None, :, :]).exp()                        # (B, t, s, H)
+    mask = torch.ones(T, T, dtype=torch.bool).tril()[None, :, :, None]
+    A = torch.einsum("bthd,bshd->btsh", q, k) * dec * mask
+    ref = 0.3 * torch.einsum("btsh,bshd->bthd", A, v)
+    assert torch.allclose(o, ref, rtol=1e-5, atol=1e-5)

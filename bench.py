@@ -341,6 +341,98 @@ def run_model(args, rank, world, local_rank, cp=False):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- GLA scorer workload
+def _peaks():
+    """Dense bf16 peak for a kernel timed on its own: the measured burst figure."""
+    try:
+        m = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        m = {}
+    if "bf16_tflops" in m:
+        return {"tflops": m["bf16_tflops"], "tf_src": "measured burst"}
+    return {"tflops": 1590.0, "tf_src": "fallback"}
+
+
+def run_scorer_gla(args, rank, world, local_rank):
+    """The `gla` scorer (SEL:692-755) at the layer configuration: simple GLA over
+    the dilated views (dilation 4: 32 sub-sequences of 32768 steps per pass),
+    both passes, then norms, level maxima and pyramid means.  Forward only (the
+    scores carry no gradient).  N ranks run independent replicas."""
+    import __graft_entry__ as ge
+    lh = ge.load_package()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, S, H, D, L, p = CFG["B"], CFG["S"], CFG["H"], CFG["D"], CFG["L"], CFG["p"]
+    di = 4
+    scorer = lh.DilatedLighthouseGLAScorer(D, dilation=di, pooling_factor=p, levels=L)
+    g = torch.Generator().manual_seed(0)
+    host = [torch.randn(B, S, H, D, generator=g).to(torch.bfloat16).pin_memory() for _ in range(3)]
+    host.append((torch.nn.functional.logsigmoid(torch.randn(B, S, H, generator=g)) / 16).pin_memory())
+    xs = [h.to(dev) for h in host]
+    T, Hd = S // di, H * di
+    view = lambda x: x.reshape(B, T, Hd, *x.shape[3:])
+    kern = lambda: lh._native.simple_gla_fwd(view(xs[0]), view(xs[1]), view(xs[2]), view(xs[3]), scorer.scaling,
+                                             q2=view(xs[1]), k2=view(xs[0]))
+    for _ in range(args.warmup):
+        scorer.scores(*xs)
+        kern()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        t0, t1 = ev(), ev()
+        t0.record()
+        for _ in range(args.steps):
+            scorer.scores(*xs)
+        t1.record()
+        k0, k1 = ev(), ev()
+        k0.record()
+        for _ in range(args.steps):
+            kern()
+        k1.record()
+        torch.cuda.synchronize()
+    ms, kms = t0.elapsed_time(t1) / args.steps, k0.elapsed_time(k1) / args.steps
+    e0, e1 = ev(), ev()
+    e0.record()
+    for _ in range(args.steps):
+        d = [h.to(dev, non_blocking=True) for h in host]
+        sqk, skq = scorer.scores(*d)
+        (sqk[0, 0, 0] + skq[0, 0, 0]).item()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    assert lh._native.device_status() == 0
+    if world > 1:
+        t = torch.tensor([ms, kms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, kms, e2e_ms = t.tolist()
+    if rank != 0:
+        return
+    # useful FLOPs per pass and (step, head): causal half of the 64x64 intra QK^T and AV,
+    # the inter-chunk Q S and the state update K^T V (128 x 128 state)
+    flops = 2 * B * Hd * T * 2 * (64 * D / 2 + 64 * D / 2 + D * D + D * D)
+    peaks = _peaks()
+    line = {
+        "metric": "GLA scorer tokens/s @S=128K (dilation 4, both passes + pyramid)", "value": B * S * world / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v, gate logsigmoid(N(0,1))/16)",
+        "config": _config({"workload": "gla_scorer_fwd", "scorer": "gla", "dilation": di,
+                           "parallelism": f"replicas x{world}"}),
+        "roofline": {"kernel": "simple_gla_fwd_kernel (warp MMA, both passes)", "bound": "tensor",
+                     "achieved": flops / (kms * 1e-3) / 1e12, "peak": peaks["tflops"], "unit": "TFLOP/s",
+                     "frac": flops / (kms * 1e-3) / 1e12 / peaks["tflops"], "peak_source": peaks["tf_src"],
+                     "traffic": None, "flops_per_launch": flops, "ms_per_launch": kms},
+        "e2e": {"value": B * S * world / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": sum(h.numel() * h.element_size() for h in host), "d2h_bytes_per_step": 4,
+                "ms_per_step": e2e_ms, "api": "DilatedLighthouseGLAScorer.scores"},
+        "gpu_launches": 3 * args.steps,          # scorer: GLA + pyramid; kernel leg: GLA
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- CPU arm
 def cpu_sample(steps: int, warmup: int):
     """The reference path on the host cores, one head of the workload per step."""
@@ -390,9 +482,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="layer", choices=["layer", "model", "model_cp"],
+    ap.add_argument("--workload", default="layer", choices=["layer", "model", "model_cp", "scorer_gla"],
                     help="layer: BASELINE config 3 (default); model: config 4, the 270M training step; "
-                         "model_cp: config 5, one sequence context-parallel over the N ranks")
+                         "model_cp: config 5, one sequence context-parallel over the N ranks; "
+                         "scorer_gla: the `gla` scorer at the layer configuration")
     ap.add_argument("--seq-len", type=int, default=None, help="profiling only: override S")
     ap.add_argument("--topk", type=int, default=None, help="profiling only: override k")
     args = ap.parse_args()
@@ -412,6 +505,8 @@ def main():
     try:
         if args.workload in ("model", "model_cp"):
             run_model(args, rank, world, local_rank, cp=args.workload == "model_cp")
+        elif args.workload == "scorer_gla":
+            run_scorer_gla(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

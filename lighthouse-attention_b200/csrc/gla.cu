@@ -14,11 +14,12 @@
 // slab of 64 columns, pass), eight warps, walking the chunks in order.  Per chunk
 //     intra  A = (Q K^T) * scale * exp(G_t - G_s) [s <= t]    (64 x 64, fp32 -> bf16)
 //     out    O = scale * exp(G_t) * (Q S_prev) + A V          (64 x 64 slab)
-//     state  S = exp(G_63) S_prev + K^T (V * exp(G_63 - G_s)) (128 x 64 slab)
+//     state  S = exp(G_63) S_prev + (K * exp(G_63 - G_s))^T V (128 x 64 slab)
 // with G chunk-local.  The products run on warp-level bf16 MMAs (m16n8k16,
 // fp32 accumulate); the next chunk's Q/K/V stream into the other half of a
-// double buffer with cp.async while the current one is computed.  The
-// bf16-rounded operands (A, V*exp, the state as the Q S operand) follow the
+// double buffer with cp.async while the current one is computed, and one
+// barrier per chunk orders the buffers.  The bf16-rounded operands (A, the
+// decayed K, the state as the Q S operand) follow the
 // precision of fla's chunked kernels.  Two (q, k, o) passes that share v and g
 // (the scorer's q->k and k->q passes) run in one launch.
 #include "lh_common.cuh"
@@ -35,9 +36,9 @@ struct Smem {
   __nv_bfloat16 q[2][C * D];   // rows of 256 B, 16-byte chunks XOR-swizzled by row
   __nv_bfloat16 k[2][C * D];
   __nv_bfloat16 v[2][C * VS];  // rows of 128 B
-  __nv_bfloat16 vt[C * VS];    // V * exp(G_63 - G_s)
   __nv_bfloat16 st[2][D * VS]; // state S (key x value) as bf16, double-buffered
-  float g2[2][C];              // chunk-local cumulative gate, times log2(e)
+  float g2[2][C];              // chunk-local cumulative gate G, times log2(e)
+  float kd[2][C];              // exp(G_63 - G_s): decay of step s to the chunk end
 };
 
 __device__ __forceinline__ uint32_t sw256(int r, int c) { return r * 256 + ((c ^ (r & 7)) << 4); }
@@ -93,8 +94,9 @@ __device__ __forceinline__ void load_chunk(Smem& sm, int buf, const Pass& ps, co
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// Warp 0: chunk-local inclusive cumulative sum of g (two values per lane), times log2(e).
-__device__ __forceinline__ void gate_scan(float* out, float a, float b, int lane) {
+// Warp 0: chunk-local inclusive cumulative sum of g (two values per lane), times
+// log2(e), and the decay of every step to the chunk end.
+__device__ __forceinline__ void gate_scan(float* out, float* kd, float a, float b, int lane) {
   constexpr float kLog2e = 1.4426950408889634f;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -102,8 +104,11 @@ __device__ __forceinline__ void gate_scan(float* out, float a, float b, int lane
     if (lane >= o) { a += x; b += y; }
   }
   b += __shfl_sync(0xffffffffu, a, 31);
+  const float last = __shfl_sync(0xffffffffu, b, 31) * kLog2e;
   out[lane] = a * kLog2e;
   out[lane + 32] = b * kLog2e;
+  kd[lane] = exp2f(last - a * kLog2e);
+  kd[lane + 32] = exp2f(last - b * kLog2e);
 }
 
 __global__ void __launch_bounds__(NT, 1)
@@ -116,7 +121,9 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
   const Pass ps = pass ? p1 : p0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 2, tq = lane & 3;                     // mma fragment row / column pair
-  const int rb = warp & 3, vh = warp >> 2;                     // output rows 16rb.., slab columns 32vh..
+  // output rows 16rb.., slab columns 32vh..; rb mirrored for vh = 1 so that the two warps of
+  // a scheduler (warp, warp + 4) hold one short and one long causal row block
+  const int vh = warp >> 2, rb = vh ? 3 - (warp & 3) : (warp & 3);
   const long long rstride = (long long)H * D;
   const long long row0 = ((long long)b * T * H + h) * D;     // element offset of (b, t = 0, h, 0)
   const int vcol = slab * VS;
@@ -130,7 +137,7 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
   if (warp == 0) {
     const float a = lane < T ? gh[(long long)lane * H] : 0.f;
     const float c = lane + 32 < T ? gh[(long long)(lane + 32) * H] : 0.f;
-    gate_scan(sm.g2[0], a, c, lane);
+    gate_scan(sm.g2[0], sm.kd[0], a, c, lane);
   }
 
   float sacc[8][4];                                            // state rows 16*warp.., 64 value columns
@@ -139,7 +146,6 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
 
   const uint32_t st_base[2] = {(uint32_t)__cvta_generic_to_shared(sm.st[0]),
                                (uint32_t)__cvta_generic_to_shared(sm.st[1])};
-  const uint32_t vt_base = (uint32_t)__cvta_generic_to_shared(sm.vt);
 
   for (int n = 0; n < n_chunks; ++n) {
     const int buf = n & 1;
@@ -158,22 +164,6 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
     const uint32_t qs = (uint32_t)__cvta_generic_to_shared(sm.q[buf]);
     const uint32_t ks = (uint32_t)__cvta_generic_to_shared(sm.k[buf]);
     const uint32_t vs = (uint32_t)__cvta_generic_to_shared(sm.v[buf]);
-
-    // V * exp(G_63 - G_s) for the state update
-    for (int i = threadIdx.x; i < C * 8; i += NT) {
-      const int r = i >> 3, c = i & 7;
-      const float f = exp2f(gl - G[r]);
-      const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(sm.v[buf]) + sw128(r, c));
-      const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&u);
-      uint4 w;
-      uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const float2 x = __bfloat1622float2(e[m]);
-        wp[m] = pack_bf16(x.x * f, x.y * f);
-      }
-      *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(sm.vt) + sw128(r, c)) = w;
-    }
 
     // ---- intra scores A = Q K^T (rows 16rb.., causal key tiles only) and O_inter = Q S_prev
     float acc[8][4], oacc[4][4];
@@ -248,9 +238,7 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
           *reinterpret_cast<uint32_t*>(ps.o + row0 + (long long)tb * rstride + col) = pack_bf16(oacc[j][2], oacc[j][3]);
       }
     }
-    __syncthreads();                                           // V * exp complete
-
-    // ---- state S = exp(G_63) S + K^T (V * exp(G_63 - G_s)); this warp: key rows 16*warp..
+    // ---- state S = exp(G_63) S + (K * exp(G_63 - G_s))^T V; this warp: key rows 16*warp..
     const float fl = exp2f(gl);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -260,10 +248,19 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
     for (int kk = 0; kk < C / 16; ++kk) {
       uint32_t a[4];
       ldsm4t(ks + sw256(16 * kk + (lane & 7) + ((lane >> 4) << 3), 2 * warp + ((lane >> 3) & 1)), a);
+      // fragment columns are steps s = 16kk + 2tq (+1) for a[0], a[1] and + 8 for a[2], a[3]
+      const float2 d0 = *reinterpret_cast<const float2*>(&sm.kd[buf][16 * kk + 2 * tq]);
+      const float2 d1 = *reinterpret_cast<const float2*>(&sm.kd[buf][16 * kk + 8 + 2 * tq]);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a[m]));
+        const float2 d = m < 2 ? d0 : d1;
+        a[m] = pack_bf16(x.x * d.x, x.y * d.y);
+      }
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
         uint32_t bb[4];
-        ldsm4t(vt_base + sw128(16 * kk + (lane & 7) + (((lane >> 3) & 1) << 3), 2 * np + (lane >> 4)), bb);
+        ldsm4t(vs + sw128(16 * kk + (lane & 7) + (((lane >> 3) & 1) << 3), 2 * np + (lane >> 4)), bb);
         mma(sacc[2 * np], a, bb[0], bb[1]);
         mma(sacc[2 * np + 1], a, bb[2], bb[3]);
       }
@@ -278,7 +275,7 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
         *reinterpret_cast<uint32_t*>(stb + sw128(r_hi, j) + 4 * tq) = pack_bf16(sacc[j][2], sacc[j][3]);
       }
     }
-    if (warp == 0 && n + 1 < n_chunks) gate_scan(sm.g2[buf ^ 1], gn0, gn1, lane);
+    if (warp == 0 && n + 1 < n_chunks) gate_scan(sm.g2[buf ^ 1], sm.kd[buf ^ 1], gn0, gn1, lane);
   }
 }
 

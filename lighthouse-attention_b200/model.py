@@ -29,7 +29,8 @@ import torch.nn.functional as F
 
 from . import _native
 from . import cp as _cp
-from .lighthouse_selection import lighthouse_attention
+from .lighthouse_selection import (DilatedLighthouseGLAScorer, DilatedLighthouseScorer, LighthouseLocal,
+                                   lighthouse_attention)
 
 
 @dataclass
@@ -49,7 +50,8 @@ class ModelArgs:
     lighthouse_num_levels: int = 3
     lighthouse_pooling_factor: int = 4
     lighthouse_topk: int = 2048
-    lighthouse_scorer: str = "norm"
+    lighthouse_scorer: str = "norm"          # "norm" | "dilated" | "gla"  (context parallelism: "norm" only)
+    dilation: int = 4
     lighthouse_full_attn_layers: list = field(default_factory=lambda: [0, 1, 28, 29])
 
 
@@ -102,9 +104,21 @@ class Attention(nn.Module):
         self.wv = nn.Linear(args.dim, args.n_heads * self.head_dim, bias=False)
         self.wo = nn.Linear(args.n_heads * self.head_dim, args.dim, bias=False)
         self.lighthouse = args.use_selection_lighthouse and layer_id not in args.lighthouse_full_attn_layers
-        if self.lighthouse and args.lighthouse_scorer != "norm":
-            raise ValueError("only the `norm` Lighthouse scorer is provided")
         self.L, self.p, self.k = args.lighthouse_num_levels, args.lighthouse_pooling_factor, args.lighthouse_topk
+        # scorer from the config (PATCH:601-637); the GLA scorer adds a per-token
+        # gate projection, gk = logsigmoid(wg(x)) / 16 (PATCH:662-664, 708-710)
+        self.scorer_name = (args.lighthouse_scorer or "norm").lower()
+        self.layer = None
+        if self.scorer_name not in ("norm", "dilated", "gla"):
+            raise ValueError(f"unknown lighthouse_scorer {args.lighthouse_scorer!r}")
+        if self.lighthouse and self.scorer_name != "norm":
+            kw = dict(dilation=args.dilation, pooling_factor=self.p, levels=self.L)
+            scorer = (DilatedLighthouseGLAScorer(self.head_dim, **kw) if self.scorer_name == "gla"
+                      else DilatedLighthouseScorer(head_dim=self.head_dim, **kw))
+            self.layer = LighthouseLocal(None, scorer, num_levels=self.L, pooling_factor=self.p, topk=self.k)
+            if self.scorer_name == "gla":
+                self.wg = nn.Linear(args.dim, args.n_heads, bias=True)
+                self.gate_logit_normalizer = 16
 
     def forward(self, x, freqs, cp_info=None):
         B, S, _ = x.shape
@@ -114,10 +128,16 @@ class Attention(nn.Module):
         xq, xk = rope_qk(xq, xk, freqs)
         if cp_info is not None:
             rank, world, group = cp_info
+            if self.layer is not None:
+                raise ValueError(f"lighthouse_scorer={self.scorer_name!r} is not supported under context "
+                                 "parallelism (PATCH:610-615); use 'norm'")
             if self.lighthouse:
                 out = _cp.lighthouse_cp_forward(xq, xk, xv, self.L, self.p, self.k, rank, world, group)
             else:
                 out = _cp.full_cp_attention(xq, xk, xv, rank, world, group)
+        elif self.layer is not None:
+            gk = F.logsigmoid(self.wg(x).float()) / self.gate_logit_normalizer if self.scorer_name == "gla" else None
+            out = self.layer(xq, xk, xv, gk=gk)
         elif self.lighthouse:
             out = lighthouse_attention(xq, xk, xv, self.L, self.p, self.k)          # (B, H, S, D)
         else:
@@ -169,9 +189,11 @@ class Transformer(nn.Module):
     def init_weights(self, seed: int = 0):
         g = torch.Generator(device="cpu").manual_seed(seed)
         for name, p in self.named_parameters():
-            if p.dim() == 2:
-                with torch.no_grad():
+            with torch.no_grad():
+                if p.dim() == 2:
                     p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+                elif name.endswith("wg.bias"):                # gate projection bias (PATCH:687-689)
+                    p.zero_()
 
     def forward(self, tokens):
         B, S = tokens.shape

@@ -4,10 +4,11 @@ import torch
 
 
 @pytest.mark.gpu
-def test_small_model_trains(lh, cuda):
+@pytest.mark.parametrize("scorer", ["norm", "dilated", "gla"])
+def test_small_model_trains(lh, cuda, scorer):
     from lighthouse_b200 import model as M
     args = M.ModelArgs(dim=256, n_layers=4, n_heads=2, n_kv_heads=2, hidden_dim=384, max_seq_len=4096,
-                       lighthouse_topk=256, lighthouse_full_attn_layers=[0])
+                       lighthouse_topk=256, lighthouse_full_attn_layers=[0], lighthouse_scorer=scorer)
     torch.manual_seed(0)
     m = M.Transformer(args).to(cuda)
     m.init_weights(0)
@@ -21,6 +22,21 @@ def test_small_model_trains(lh, cuda):
     assert losses[-1] < losses[0] - 0.5, losses
     assert lh._native.device_status() == 0
     assert sum(1 for layer in m.layers if layer.attention.lighthouse) == 3
+    if scorer == "gla":           # the gate only feeds the selection: no gradient reaches it
+        assert all(layer.attention.wg.weight.grad is None for layer in m.layers[1:])
+
+
+def test_non_norm_scorers_refuse_context_parallelism(lh):
+    from lighthouse_b200 import model as M
+    for scorer in ("dilated", "gla"):
+        args = M.ModelArgs(dim=256, n_layers=2, n_heads=2, n_kv_heads=2, hidden_dim=384,
+                           lighthouse_full_attn_layers=[], lighthouse_scorer=scorer)
+        attn = M.Attention(args, 0)
+        x = torch.randn(1, 64, 256)
+        with pytest.raises(ValueError, match="context"):
+            attn(x, M.rope_freqs(128, 64, 1e4, "cpu"), cp_info=(0, 2, None))
+    with pytest.raises(ValueError):
+        M.Attention(M.ModelArgs(lighthouse_scorer="bogus"), 3)
 
 
 def test_flavour_is_270m(lh):

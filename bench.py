@@ -430,6 +430,19 @@ def run_scorer_gla(args, rank, world, local_rank):
         "gpu_launches": 3 * args.steps,          # scorer: GLA + pyramid; kernel leg: GLA
         "clocks": clk.summary(),
     }
+    if world == 1 and not args.no_cpu_baseline:
+        # the oracle (fp32 recurrence, ATen on the host threads) on the first 8192 tokens;
+        # its cost is linear in the sequence length, so tokens/s carries over
+        from oracle import oracle as O
+        n = 8192
+        cs = [h[:, :n].float() for h in host[:3]] + [host[3][:, :n]]
+        t = time.perf_counter()
+        O.gla_scorer(*cs, di, p, L)
+        dt = time.perf_counter() - t
+        line["cpu_baseline"] = {"value": B * n / dt, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                                "kind": "port", "dtype": "f32",
+                                "sample": f"first {n} of {S} tokens, all heads, both passes + pyramid; oracle "
+                                          "recurrence (fla's published simple-GLA definition)"}
     print(json.dumps(line), flush=True)
 
 

@@ -409,9 +409,9 @@ def run_scorer_gla(args, rank, world, local_rank):
         ms, kms, e2e_ms = t.tolist()
     if rank != 0:
         return
-    # useful FLOPs per pass and (step, head): causal half of the 64x64 intra QK^T and AV,
-    # the inter-chunk Q S and the state update K^T V (128 x 128 state)
-    flops = 2 * B * Hd * T * 2 * (64 * D / 2 + 64 * D / 2 + D * D + D * D)
+    # algorithmic FLOPs: the recurrence's state update k v^T and read-out q S, 2 D^2 multiply-adds
+    # per (step, sub-head, pass); the chunked evaluation's intra-chunk products are extra work
+    flops = 2 * B * Hd * T * 4 * D * D
     peaks = _peaks()
     line = {
         "metric": "GLA scorer tokens/s @S=128K (dilation 4, both passes + pyramid)", "value": B * S * world / (ms * 1e-3),

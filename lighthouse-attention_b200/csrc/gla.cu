@@ -9,12 +9,12 @@
 // with a zero initial state.  Layout (B, T, H, D), D = 128, bf16 in and out,
 // fp32 gate (B, T, H).
 //
-// This kernel evaluates it chunk by chunk (64 time steps) with the state held
+// This kernel evaluates it chunk by chunk (C = 128 time steps) with the state held
 // in fp32 registers for the whole sequence: one CTA per (batch, head, value
 // slab of 64 columns, pass), eight warps, walking the chunks in order.  Per chunk
-//     intra  A = (Q K^T) * scale * exp(G_t - G_s) [s <= t]    (64 x 64, fp32 -> bf16)
-//     out    O = scale * exp(G_t) * (Q S_prev) + A V          (64 x 64 slab)
-//     state  S = exp(G_63) S_prev + (K * exp(G_63 - G_s))^T V (128 x 64 slab)
+//     intra  A = (Q K^T) * scale * exp(G_t - G_s) [s <= t]        (C x C, fp32 -> bf16)
+//     out    O = scale * exp(G_t) * (Q S_prev) + A V              (C x 64 slab)
+//     state  S = exp(G_end) S_prev + (K * exp(G_end - G_s))^T V   (128 x 64 slab)
 // with G chunk-local.  The products run on warp-level bf16 MMAs (m16n8k16,
 // fp32 accumulate); the next chunk's Q/K/V stream into the other half of a
 // double buffer with cp.async while the current one is computed, and one
@@ -27,10 +27,17 @@
 namespace lh {
 namespace gla {
 
-constexpr int C = 64;          // chunk length (time steps)
+#ifndef LH_GLA_CHUNK
+#define LH_GLA_CHUNK 128
+#endif
+constexpr int C = LH_GLA_CHUNK; // chunk length (time steps): 64 or 128 (128 is faster: half the sequential steps)
 constexpr int D = 128;         // head dim (key dim)
 constexpr int VS = 64;         // value columns per CTA
-constexpr int NT = 256;        // threads
+constexpr int NT = 256;        // threads: eight warps
+constexpr int NRB = C / 16;    // 16-row blocks of a chunk
+constexpr int VH = 8 / NRB;    // warps sharing one row block (each takes VS / VH value columns)
+constexpr int NO = VS / VH / 8; // 8-column output tiles per warp
+static_assert(C == 64 || C == 128, "chunk of 64 or 128 steps");
 
 struct Smem {
   __nv_bfloat16 q[2][C * D];   // rows of 256 B, 16-byte chunks XOR-swizzled by row
@@ -38,7 +45,7 @@ struct Smem {
   __nv_bfloat16 v[2][C * VS];  // rows of 128 B
   __nv_bfloat16 st[2][D * VS]; // state S (key x value) as bf16, double-buffered
   float g2[2][C];              // chunk-local cumulative gate G, times log2(e)
-  float kd[2][C];              // exp(G_63 - G_s): decay of step s to the chunk end
+  float kd[2][C];              // exp(G_end - G_s): decay of step s to the chunk end
 };
 
 __device__ __forceinline__ uint32_t sw256(int r, int c) { return r * 256 + ((c ^ (r & 7)) << 4); }
@@ -94,21 +101,26 @@ __device__ __forceinline__ void load_chunk(Smem& sm, int buf, const Pass& ps, co
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// Warp 0: chunk-local inclusive cumulative sum of g (two values per lane), times
-// log2(e), and the decay of every step to the chunk end.
-__device__ __forceinline__ void gate_scan(float* out, float* kd, float a, float b, int lane) {
+// Warp 0: chunk-local inclusive cumulative sum of g (lane holds steps lane + 32 i),
+// times log2(e), and the decay of every step to the chunk end.
+__device__ __forceinline__ void gate_scan(float* out, float* kd, float (&x)[C / 32], int lane) {
   constexpr float kLog2e = 1.4426950408889634f;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const float x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b, o);
-    if (lane >= o) { a += x; b += y; }
+#pragma unroll
+    for (int i = 0; i < C / 32; ++i) {
+      const float y = __shfl_up_sync(0xffffffffu, x[i], o);
+      if (lane >= o) x[i] += y;
+    }
   }
-  b += __shfl_sync(0xffffffffu, a, 31);
-  const float last = __shfl_sync(0xffffffffu, b, 31) * kLog2e;
-  out[lane] = a * kLog2e;
-  out[lane + 32] = b * kLog2e;
-  kd[lane] = exp2f(last - a * kLog2e);
-  kd[lane + 32] = exp2f(last - b * kLog2e);
+#pragma unroll
+  for (int i = 1; i < C / 32; ++i) x[i] += __shfl_sync(0xffffffffu, x[i - 1], 31);
+  const float last = __shfl_sync(0xffffffffu, x[C / 32 - 1], 31) * kLog2e;
+#pragma unroll
+  for (int i = 0; i < C / 32; ++i) {
+    out[lane + 32 * i] = x[i] * kLog2e;
+    kd[lane + 32 * i] = exp2f(last - x[i] * kLog2e);
+  }
 }
 
 __global__ void __launch_bounds__(NT, 1)
@@ -121,9 +133,11 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
   const Pass ps = pass ? p1 : p0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 2, tq = lane & 3;                     // mma fragment row / column pair
-  // output rows 16rb.., slab columns 32vh..; rb mirrored for vh = 1 so that the two warps of
-  // a scheduler (warp, warp + 4) hold one short and one long causal row block
-  const int vh = warp >> 2, rb = vh ? 3 - (warp & 3) : (warp & 3);
+  // output rows 16rb.., slab columns vh * VS / VH..; rb mirrored for the upper four warps so
+  // that the two warps of a scheduler (warp, warp + 4) hold one short and one long causal block
+  const int half = warp >> 2;
+  const int rb = half ? NRB - 1 - (warp & 3) : (warp & 3);
+  const int vh = VH == 2 ? half : 0;
   const long long rstride = (long long)H * D;
   const long long row0 = ((long long)b * T * H + h) * D;     // element offset of (b, t = 0, h, 0)
   const int vcol = slab * VS;
@@ -133,11 +147,11 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
   // zero state operand for chunk 0 (it reads buffer 1)
   for (int i = threadIdx.x; i < D * VS / 2; i += NT) reinterpret_cast<uint32_t*>(sm.st[1])[i] = 0u;
   load_chunk(sm, 0, ps, v, 0, T, row0, rstride, vcol);
-  float gn0 = 0.f, gn1 = 0.f;                                  // warp 0: gate of the next chunk
+  float gn[C / 32];                                             // warp 0: gate of the next chunk
   if (warp == 0) {
-    const float a = lane < T ? gh[(long long)lane * H] : 0.f;
-    const float c = lane + 32 < T ? gh[(long long)(lane + 32) * H] : 0.f;
-    gate_scan(sm.g2[0], sm.kd[0], a, c, lane);
+#pragma unroll
+    for (int i = 0; i < C / 32; ++i) gn[i] = lane + 32 * i < T ? gh[(long long)(lane + 32 * i) * H] : 0.f;
+    gate_scan(sm.g2[0], sm.kd[0], gn, lane);
   }
 
   float sacc[8][4];                                            // state rows 16*warp.., 64 value columns
@@ -155,8 +169,9 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
       load_chunk(sm, buf ^ 1, ps, v, n + 1, T, row0, rstride, vcol);
       if (warp == 0) {
         const int t0 = (n + 1) * C;
-        gn0 = t0 + lane < T ? gh[(long long)(t0 + lane) * H] : 0.f;
-        gn1 = t0 + lane + 32 < T ? gh[(long long)(t0 + lane + 32) * H] : 0.f;
+#pragma unroll
+        for (int i = 0; i < C / 32; ++i)
+          gn[i] = t0 + lane + 32 * i < T ? gh[(long long)(t0 + lane + 32 * i) * H] : 0.f;
       }
     }
     const float* G = sm.g2[buf];
@@ -166,18 +181,18 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
     const uint32_t vs = (uint32_t)__cvta_generic_to_shared(sm.v[buf]);
 
     // ---- intra scores A = Q K^T (rows 16rb.., causal key tiles only) and O_inter = Q S_prev
-    float acc[8][4], oacc[4][4];
+    float acc[2 * NRB][4], oacc[NO][4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int j = 0; j < 2 * NRB; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
+    for (int j = 0; j < NO; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
     const uint32_t stp = buf ? st_base[0] : st_base[1];
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       uint32_t a[4];
       ldsm4(qs + sw256(16 * rb + (lane & 15), 2 * kk + (lane >> 4)), a);
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {
+      for (int np = 0; np < NRB; ++np) {
         if (np > rb) break;                                    // key tiles past the diagonal are masked
         uint32_t bb[4];
         ldsm4(ks + sw256(16 * np + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), bb);
@@ -185,9 +200,9 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
         mma(acc[2 * np + 1], a, bb[2], bb[3]);
       }
 #pragma unroll
-      for (int np = 0; np < 2; ++np) {
+      for (int np = 0; np < NO / 2; ++np) {
         uint32_t bb[4];
-        ldsm4t(stp + sw128(16 * kk + (lane & 7) + (((lane >> 3) & 1) << 3), 4 * vh + 2 * np + (lane >> 4)), bb);
+        ldsm4t(stp + sw128(16 * kk + (lane & 7) + (((lane >> 3) & 1) << 3), NO * vh + 2 * np + (lane >> 4)), bb);
         mma(oacc[2 * np], a, bb[0], bb[1]);
         mma(oacc[2 * np + 1], a, bb[2], bb[3]);
       }
@@ -197,12 +212,12 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
     const float g_lo = G[t_lo], g_hi = G[t_hi];
     const float f_lo = scale * exp2f(g_lo), f_hi = scale * exp2f(g_hi);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < NO; ++j) {
       oacc[j][0] *= f_lo; oacc[j][1] *= f_lo; oacc[j][2] *= f_hi; oacc[j][3] *= f_hi;
     }
-    uint32_t af[4][4];                                         // A as bf16 operand fragments, k-steps 0..rb
+    uint32_t af[NRB][4];                                       // A as bf16 operand fragments, k-steps 0..rb
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 2 * NRB; ++j) {
       if ((j >> 1) > rb) break;
       const int s0 = 8 * j + 2 * tq, s1 = s0 + 1;
       const float gs0 = G[s0], gs1 = G[s1];
@@ -215,30 +230,30 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
     }
     // ---- O += A V (k-steps over the causal key tiles)
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
+    for (int kk = 0; kk < NRB; ++kk) {
       if (kk > rb) break;
       const uint32_t a[4] = {af[kk][0], af[kk][1], af[kk][2], af[kk][3]};
 #pragma unroll
-      for (int np = 0; np < 2; ++np) {
+      for (int np = 0; np < NO / 2; ++np) {
         uint32_t bb[4];
-        ldsm4t(vs + sw128(16 * kk + (lane & 7) + (((lane >> 3) & 1) << 3), 4 * vh + 2 * np + (lane >> 4)), bb);
+        ldsm4t(vs + sw128(16 * kk + (lane & 7) + (((lane >> 3) & 1) << 3), NO * vh + 2 * np + (lane >> 4)), bb);
         mma(oacc[2 * np], a, bb[0], bb[1]);
         mma(oacc[2 * np + 1], a, bb[2], bb[3]);
       }
     }
-    // ---- store O (bf16): rows t_lo / t_hi, columns vcol + 32vh + 8j + 2tq
+    // ---- store O (bf16): rows t_lo / t_hi, columns vcol + 8 (NO vh + j) + 2tq
     {
       const int ta = n * C + t_lo, tb = n * C + t_hi;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int col = vcol + 32 * vh + 8 * j + 2 * tq;
+      for (int j = 0; j < NO; ++j) {
+        const int col = vcol + 8 * (NO * vh + j) + 2 * tq;
         if (ta < T)
           *reinterpret_cast<uint32_t*>(ps.o + row0 + (long long)ta * rstride + col) = pack_bf16(oacc[j][0], oacc[j][1]);
         if (tb < T)
           *reinterpret_cast<uint32_t*>(ps.o + row0 + (long long)tb * rstride + col) = pack_bf16(oacc[j][2], oacc[j][3]);
       }
     }
-    // ---- state S = exp(G_63) S + (K * exp(G_63 - G_s))^T V; this warp: key rows 16*warp..
+    // ---- state S = exp(G_end) S + (K * exp(G_end - G_s))^T V; this warp: key rows 16*warp..
     const float fl = exp2f(gl);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -275,7 +290,7 @@ simple_gla_fwd_kernel(Pass p0, Pass p1, const __nv_bfloat16* __restrict__ v, con
         *reinterpret_cast<uint32_t*>(stb + sw128(r_hi, j) + 4 * tq) = pack_bf16(sacc[j][2], sacc[j][3]);
       }
     }
-    if (warp == 0 && n + 1 < n_chunks) gate_scan(sm.g2[buf ^ 1], sm.kd[buf ^ 1], gn0, gn1, lane);
+    if (warp == 0 && n + 1 < n_chunks) gate_scan(sm.g2[buf ^ 1], sm.kd[buf ^ 1], gn, lane);
   }
 }
 

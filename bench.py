@@ -502,7 +502,7 @@ def main():
     ap.add_argument("--seq-len", type=int, default=None, help="profiling only: override S")
     ap.add_argument("--topk", type=int, default=None, help="profiling only: override k")
     args = ap.parse_args()
-    if args.seq_len and args.workload == "layer":
+    if args.seq_len and args.workload in ("layer", "scorer_gla"):
         CFG["S"] = args.seq_len
     if args.topk:
         CFG["k"] = args.topk

@@ -10,6 +10,7 @@ or INTEGRATION.md).  Modules:
   _native                    ctypes binding of liblighthouse_b200.so (include/lighthouse_b200.h)
 """
 from . import _native  # noqa: F401
+from . import library  # noqa: F401  (registers the lighthouse_b200:: custom ops)
 from .lighthouse_selection import (DialatedLighthouseNormScorer, DialatedLighthouseNormScorerCP,  # noqa: F401
                                    DilatedLighthouseGLAScorer, DilatedLighthouseScorer, LighthouseCP,
                                    LighthouseLocal, compute_output_indices_selection, lighthouse_attention,

@@ -26,6 +26,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _native
+from .library import ops as _ops
 from .lighthouse_selection_cuda import (LighthouseSelectionQkKqChunkedTopkNvrtc,  # noqa: F401
                                         compute_output_indices_selection)
 
@@ -44,7 +45,7 @@ class _PyramidFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, xq, xk, xv, L, p):
         B, S, H, D = xq.shape
-        pq, pk, pv, sqk, skq = _native.pyramid_score(xq, xk, xv, L, p)
+        pq, pk, pv, sqk, skq = _ops.pyramid_score(xq, xk, xv, L, p)
         cat = lambda x, pooled: torch.cat([x.transpose(1, 2), pooled], dim=2)
         ctx.L, ctx.p, ctx.S = L, p, S
         ctx.mark_non_differentiable(sqk, skq)
@@ -52,11 +53,11 @@ class _PyramidFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, _gs1, _gs2, gq, gk, gv):
-        S_tot = gq.shape[2] if gq is not None else (gk if gk is not None else gv).shape[2]
-        B, H = (gq if gq is not None else (gk if gk is not None else gv)).shape[:2]
-        dev = (gq if gq is not None else (gk if gk is not None else gv)).device
-        ident = torch.arange(S_tot, dtype=torch.int32, device=dev).expand(B, H, S_tot).contiguous()
-        dq, dk, dv = _native.unpool_bwd([gq, gk, gv], ident, ctx.S, ctx.L, ctx.p)
+        given = next(g for g in (gq, gk, gv) if g is not None)
+        B, H, S_tot = given.shape[:3]
+        gq, gk, gv = (torch.zeros_like(given) if g is None else g for g in (gq, gk, gv))
+        ident = torch.arange(S_tot, dtype=torch.int32, device=given.device).expand(B, H, S_tot).contiguous()
+        dq, dk, dv = _ops.unpool_bwd(gq, gk, gv, ident, ctx.S, ctx.L, ctx.p)
         return dq, dk, dv, None, None
 
 
@@ -90,7 +91,7 @@ def _causal_attention(q, k, v):
     """(B, H, S, D) causal attention: this package's tcgen05 kernel for bf16 with
     D = 128, scaled_dot_product_attention otherwise."""
     if q.dtype == torch.bfloat16 and q.shape[-1] == 128 and q.is_cuda:
-        o, _ = _native.attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), 1.0 / math.sqrt(q.shape[-1]))
+        o, _ = _ops.attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), 1.0 / math.sqrt(q.shape[-1]))
         return o
     return F.scaled_dot_product_attention(q, k, v, is_causal=True)
 
@@ -131,7 +132,7 @@ class DilatedLighthouseScorer(nn.Module):
             out_kq = back(self.attention(view(xk), view(xq), view(xv)))
             # norms of the outputs, rounded to the dtype, max-pooled per level:
             # what the pyramid kernel computes for its first two inputs
-            _, _, _, sqk, skq = _native.pyramid_score(out_qk, out_kq, out_kq, self.levels, self.pooling_factor)
+            _, _, _, sqk, skq = _ops.pyramid_score(out_qk, out_kq, out_kq, self.levels, self.pooling_factor)
         return sqk, skq
 
     def forward(self, xq, xk, xv):
@@ -171,10 +172,11 @@ class DilatedLighthouseGLAScorer(nn.Module):
         with torch.no_grad():
             view = lambda x: x.reshape(b, s // di, di * h, d)          # fla's (B, T, H, D) layout
             gd = gk.detach().reshape(b, s // di, di * h)
-            o_qk, o_kq = _native.simple_gla_fwd(view(xq), view(xk), view(xv), gd, self.scaling,
-                                                q2=view(xk), k2=view(xq))
+            o_qk, o_kq = _ops.simple_gla_fwd2(view(xq).contiguous(), view(xk).contiguous(), view(xv).contiguous(),
+                                              gd.float().contiguous(), self.scaling, view(xk).contiguous(),
+                                              view(xq).contiguous())
             o_qk, o_kq = o_qk.view(b, s, h, d), o_kq.view(b, s, h, d)
-            _, _, _, sqk, skq = _native.pyramid_score(o_qk, o_kq, o_kq, self.levels, self.pooling_factor)
+            _, _, _, sqk, skq = _ops.pyramid_score(o_qk, o_kq, o_kq, self.levels, self.pooling_factor)
         return sqk, skq
 
     def forward(self, xq, xk, xv, gk):
@@ -188,15 +190,15 @@ class _ScatterFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, attn, indices, N_shard, N_total, L, p):
         idx = indices.to(torch.int32).contiguous()
-        inv = _native.build_inverse(idx, _native.pyramid_len(N_shard, L, p))
+        inv = _ops.build_inverse(idx, _native.pyramid_len(N_shard, L, p))
         ctx.save_for_backward(idx)
         ctx.args = (N_shard, N_total, L, p)
-        return _native.scatter_fwd(attn, inv, N_shard, N_total, L, p)
+        return _ops.scatter_fwd(attn.contiguous(), inv, N_shard, N_total, L, p)
 
     @staticmethod
     def backward(ctx, dout):
         (idx,) = ctx.saved_tensors
-        return _native.scatter_bwd(dout, idx, *ctx.args), None, None, None, None, None
+        return _ops.scatter_bwd(dout.contiguous(), idx, *ctx.args), None, None, None, None, None
 
 
 def scatter_to_base_sequence(attn_out, indices_hp, rank_ids_hp, N_shard: int, N_total: int, num_levels: int,
@@ -219,14 +221,14 @@ class _LighthouseLayerFn(torch.autograd.Function):
     def forward(ctx, xq, xk, xv, L, p, k, scores=None):
         B, S, H, D = xq.shape
         xq, xk, xv = xq.contiguous(), xk.contiguous(), xv.contiguous()
-        pq, pk, pv, sqk, skq = _native.pyramid_score(xq, xk, xv, L, p)
+        pq, pk, pv, sqk, skq = _ops.pyramid_score(xq, xk, xv, L, p)
         if scores is not None:                  # another scorer's (qk, kq) scores, fp32
             sqk, skq = (t.to(torch.float32).contiguous() for t in scores)
-        idx, inv = _native.select_topk(sqk, skq, L, p, k, S)
-        qs, ks, vs = _native.gather_selected([xq, xk, xv], [pq, pk, pv], idx)
+        idx, inv = _ops.select_topk(sqk, skq, L, p, k, S)
+        qs, ks, vs = _ops.gather_selected(xq, xk, xv, pq, pk, pv, idx)
         scale = 1.0 / math.sqrt(D)
-        o, lse = _native.attn_fwd(qs, ks, vs, scale)
-        out = _native.scatter_fwd(o, inv, S, S, L, p)
+        o, lse = _ops.attn_fwd(qs, ks, vs, scale)
+        out = _ops.scatter_fwd(o, inv, S, S, L, p)
         ctx.save_for_backward(qs, ks, vs, o, lse, idx, inv)
         ctx.args = (S, L, p, scale)
         ctx.mark_non_differentiable(idx)
@@ -236,9 +238,9 @@ class _LighthouseLayerFn(torch.autograd.Function):
     def backward(ctx, dout, _didx):
         qs, ks, vs, o, lse, idx, inv = ctx.saved_tensors
         S, L, p, scale = ctx.args
-        dattn = _native.scatter_bwd(dout, idx, S, S, L, p)
-        dqs, dks, dvs = _native.attn_bwd(qs, ks, vs, o, lse, dattn, scale)
-        dxq, dxk, dxv = _native.unpool_bwd([dqs, dks, dvs], inv, S, L, p)
+        dattn = _ops.scatter_bwd(dout.contiguous(), idx, S, S, L, p)
+        dqs, dks, dvs = _ops.attn_bwd(qs, ks, vs, o, lse, dattn, scale)
+        dxq, dxk, dxv = _ops.unpool_bwd(dqs, dks, dvs, inv, S, L, p)
         return dxq, dxk, dxv, None, None, None, None
 
 

@@ -27,7 +27,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import _native
+from .library import ops as _ops
 from . import cp as _cp
 from .lighthouse_selection import (DilatedLighthouseGLAScorer, DilatedLighthouseScorer, LighthouseLocal,
                                    lighthouse_attention)
@@ -75,12 +75,12 @@ class _RopeFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, xq, xk, table):
         ctx.save_for_backward(table)
-        return _native.rope_apply(xq, xk, table)
+        return _ops.rope_apply(xq.contiguous(), xk.contiguous(), table)
 
     @staticmethod
     def backward(ctx, gq, gk):
         (table,) = ctx.saved_tensors
-        dq, dk = _native.rope_apply(gq, gk, table, inverse=True)
+        dq, dk = _ops.rope_apply(gq.contiguous(), gk.contiguous(), table, True)
         return dq, dk, None
 
 

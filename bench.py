@@ -211,10 +211,16 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e_steps
 
+    clocks = clk.summary()
+    per_rank = None
     if world > 1:
-        t = torch.tensor([ms, e2e_ms, fwd_ms, bwd_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, e2e_ms, fwd_ms, bwd_ms = t.tolist()
+        # every rank's figures, so that a slow GPU setting the max shows by itself
+        mine = torch.tensor([ms, e2e_ms, fwd_ms, bwd_ms, float(clocks["sm_mhz"] or 0)], device=dev)
+        allr = torch.empty(world, mine.numel(), device=dev)
+        torch.distributed.all_gather_into_tensor(allr, mine)
+        per_rank = [{"ms_per_step": r[0], "e2e_ms": r[1], "attn_fwd_ms": r[2], "attn_bwd_ms": r[3], "sm_mhz": r[4]}
+                    for r in allr.tolist()]
+        ms, e2e_ms, fwd_ms, bwd_ms = allr[:, :4].max(dim=0).values.tolist()
     if rank != 0:
         return
 
@@ -256,8 +262,10 @@ def run_ours(args, rank, world, local_rank):
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms, "api": "lighthouse_attention",
                 "input_pipeline": "step i+1 host->device copy on a second stream during step i"},
         "gpu_launches": 10 * args.steps,
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }
+    if per_rank:
+        line["per_rank"] = per_rank
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(steps=2, warmup=1)["cpu_baseline"]   # warm, as the reference arm
     print(json.dumps(line), flush=True)
@@ -339,6 +347,93 @@ def run_model(args, rank, world, local_rank, cp=False):
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- sweep workload
+# S=131072 with top-k, levels and pooling factor varied.  The
+# reference kernel is defined at S=131072 only for p=4, L=3, k in {2048, 4096};
+# every other point runs at S=98304, the reference's own seq_len, where all of
+# them are defined (the package raises LighthouseShapeError, as the reference
+# writes holes, on undefined shapes).
+SWEEP = [  # (S, L, p, k)
+    (131072, 3, 4, 2048), (131072, 3, 4, 4096),
+    (98304, 3, 4, 1536), (98304, 3, 4, 2048), (98304, 3, 4, 3072), (98304, 3, 4, 4096), (98304, 3, 4, 6144),
+    (98304, 3, 2, 1536), (98304, 4, 2, 1536), (98304, 5, 2, 1536),
+    (98304, 3, 8, 1536),
+]
+
+
+def run_sweep(args, rank, world, local_rank):
+    """One line per sweep point: layer fwd+bwd tokens/s on resident inputs and the
+    attention kernels' TFLOP/s.  Inputs are drawn on the device (timing only; parity
+    of these shapes is covered by the GPU tests)."""
+    import __graft_entry__ as ge
+    lh = ge.load_package()
+    N = lh._native
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, H, D = CFG["B"], CFG["H"], CFG["D"]
+    scale = 1.0 / math.sqrt(D)
+    g = torch.Generator(device=dev).manual_seed(0)
+    for (S, L, p, k) in SWEEP:
+        xq, xk, xv = (torch.randn(B, S, H, D, generator=g, device=dev, dtype=torch.bfloat16) for _ in range(3))
+        dout = torch.randn(B, H, S, D, generator=g, device=dev, dtype=torch.bfloat16)
+        ev = {n: [] for n in ("f0", "f1", "b0", "b1")}
+
+        def step(timed):
+            pq, pk, pv, sqk, skq = N.pyramid_score(xq, xk, xv, L, p)
+            idx, inv = N.select_topk(sqk, skq, L, p, k, S)
+            qs, ks, vs = N.gather_selected([xq, xk, xv], [pq, pk, pv], idx)
+            marks = []
+            for name in ("f0", "f1", "b0", "b1"):
+                marks.append(torch.cuda.Event(enable_timing=True))
+                if timed:
+                    ev[name].append(marks[-1])
+            marks[0].record()
+            o, lse = N.attn_fwd(qs, ks, vs, scale)
+            marks[1].record()
+            out = N.scatter_fwd(o, inv, S, S, L, p)
+            dattn = N.scatter_bwd(dout, idx, S, S, L, p)
+            marks[2].record()
+            dqs, dks, dvs = N.attn_bwd(qs, ks, vs, o, lse, dattn, scale)
+            marks[3].record()
+            N.unpool_bwd([dqs, dks, dvs], inv, S, L, p)
+
+        for _ in range(args.warmup):
+            step(False)
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step(True)
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / args.steps
+        fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ev["f0"], ev["f1"]))
+        bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ev["b0"], ev["b1"]))
+        if world > 1:
+            t = torch.tensor([ms, fwd_ms, bwd_ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms, fwd_ms, bwd_ms = t.tolist()
+        assert N.device_status() == 0, "an attention kernel left a bounded wait"
+        del xq, xk, xv, dout
+        if rank != 0:
+            continue
+        S_sel = _sel_len(S, L, p, k)
+        P = S_sel * (S_sel + 1) / 2
+        print(json.dumps({
+            "metric": "Lighthouse attn fwd+bwd tokens/s (sweep point)", "value": B * S * world / (ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded N(0,1) on the device)",
+            "config": {"workload": "lighthouse_layer_sweep", "seq_len": S, "levels": L, "pooling_factor": p,
+                       "topk": k, "selected_len": S_sel, "batch": B, "heads": H, "head_dim": D,
+                       "l2": "inputs larger than L2 (no flush needed)"},
+            "kernels": {"attn_fwd_ms": fwd_ms, "attn_fwd_tflops": 4 * B * H * D * P / (fwd_ms * 1e-3) / 1e12,
+                        "attn_bwd_ms": bwd_ms, "attn_bwd_tflops": 10 * B * H * D * P / (bwd_ms * 1e-3) / 1e12,
+                        "rest_ms": ms - fwd_ms - bwd_ms},
+        }), flush=True)
 
 
 # ----------------------------------------------------------------------------- GLA scorer workload
@@ -428,8 +523,10 @@ def run_scorer_gla(args, rank, world, local_rank):
                 "h2d_bytes_per_step": sum(h.numel() * h.element_size() for h in host), "d2h_bytes_per_step": 4,
                 "ms_per_step": e2e_ms, "api": "DilatedLighthouseGLAScorer.scores"},
         "gpu_launches": 3 * args.steps,          # scorer: GLA + pyramid; kernel leg: GLA
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }
+    if per_rank:
+        line["per_rank"] = per_rank
     if world == 1 and not args.no_cpu_baseline:
         # the oracle (fp32 recurrence, ATen on the host threads) on the first 8192 tokens;
         # its cost is linear in the sequence length, so tokens/s carries over
@@ -495,10 +592,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="layer", choices=["layer", "model", "model_cp", "scorer_gla"],
+    ap.add_argument("--workload", default="layer", choices=["layer", "model", "model_cp", "scorer_gla", "sweep"],
                     help="layer: BASELINE config 3 (default); model: config 4, the 270M training step; "
                          "model_cp: config 5, one sequence context-parallel over the N ranks; "
-                         "scorer_gla: the `gla` scorer at the layer configuration")
+                         "scorer_gla: the `gla` scorer at the layer configuration; "
+                         "sweep: config 3's k / L / p sweep, one line per point")
     ap.add_argument("--seq-len", type=int, default=None, help="profiling only: override S")
     ap.add_argument("--topk", type=int, default=None, help="profiling only: override k")
     args = ap.parse_args()
@@ -518,6 +616,8 @@ def main():
     try:
         if args.workload in ("model", "model_cp"):
             run_model(args, rank, world, local_rank, cp=args.workload == "model_cp")
+        elif args.workload == "sweep":
+            run_sweep(args, rank, world, local_rank)
         elif args.workload == "scorer_gla":
             run_scorer_gla(args, rank, world, local_rank)
         else:

@@ -20,22 +20,37 @@ namespace lh {
 
 constexpr int kPyrThreads = 128;
 
+constexpr int kPyrU = 4;                 // tokens per load batch
+constexpr int kPyrStages = 4;            // batches in flight per thread
+
+__device__ __forceinline__ void pyr_cp16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0));
+}
+__device__ __forceinline__ void pyr_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
 // blockIdx.z selects the tensor (0 = q, 1 = k, 2 = v): each thread carries the
 // level accumulators of one tensor only, and q / k threads also produce that
-// tensor's norm scores.  Loads are double-buffered: the next U tokens are in
-// flight (as raw 16-byte chunks, converted when used) while the current ones
-// are reduced.
+// tensor's norm scores.  Loads go through a per-thread ring in shared memory:
+// kPyrStages batches of kPyrU tokens (16 tokens, 256 bytes per thread) are in
+// flight by cp.async while the oldest batch is reduced.  A thread only reads
+// back the chunks it copied itself, so the ring needs no barrier, and the
+// in-flight data holds no registers (more CTAs per SM than a register
+// double buffer: 6 per SM at 80 registers for L <= 3).
 template <class T, int D, int LV>
-__global__ void __launch_bounds__(kPyrThreads)
+__global__ void __launch_bounds__(kPyrThreads, LV <= 3 ? 6 : 4)
 pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T* __restrict__ xv,
                      int S, int H, int p_shift, int tpc,
                      T* __restrict__ pq, T* __restrict__ pk, T* __restrict__ pv,
                      float* __restrict__ sqk, float* __restrict__ skq, Pyramid pyr, int S_pool) {
   constexpr int VEC = Vec16<T>::N;       // elements per 16-byte chunk
   constexpr int LPH = D / VEC;           // lanes per head row
-  constexpr int U = 4;                   // tokens per load batch (8 needs ~200 registers and is slower)
+  constexpr int U = kPyrU;
+  constexpr int NST = kPyrStages;
   static_assert(LPH <= 32 && (32 % LPH) == 0, "head row must fit a warp segment");
-  extern __shared__ float s_scores[];    // [H][tpc_tot]
+  extern __shared__ __align__(16) uint8_t s_dyn[];
+  const uint4* ring = reinterpret_cast<const uint4*>(s_dyn);                    // [NST][U][threads]
+  const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(s_dyn);
+  float* s_scores = reinterpret_cast<float*>(s_dyn + (size_t)NST * U * kPyrThreads * 16);  // [H][tpc_tot]
   const int which = blockIdx.z;
   const T* x = which == 0 ? xq : (which == 1 ? xk : xv);
   T* px = which == 0 ? pq : (which == 1 ? pk : pv);
@@ -65,19 +80,22 @@ pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T
 #pragma unroll
       for (int e = 0; e < VEC; ++e) acc[l][e] = 0.f;
     }
-    // raw 16-byte chunks in flight (4 registers each); converted when used
-    uint4 raw[2][U];
-    auto load_batch = [&](int slot, int i0) {
+    // batch n of this thread's tokens -> ring stage n % NST (zero-filled past the end)
+    auto issue = [&](int n) {
+      const int st = n % NST;
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-        raw[slot][u] = (active && i0 + u < ntok)
-                           ? __ldg(reinterpret_cast<const uint4*>(src + (size_t)(i0 + u) * tok_stride))
-                           : make_uint4(0u, 0u, 0u, 0u);
+      for (int u = 0; u < U; ++u) {
+        const int i = n * U + u;
+        const bool ok = active && i < ntok;
+        pyr_cp16(ring_s + (uint32_t)(((st * U + u) * kPyrThreads + threadIdx.x) * 16),
+                 ok ? (const void*)(src + (size_t)i * tok_stride) : (const void*)x, ok);
+      }
     };
-    auto process = [&](int slot, int i0) {
+    auto process = [&](int n) {
+      const int st = n % NST, i0 = n * U;
       float buf[U][VEC];
 #pragma unroll
-      for (int u = 0; u < U; ++u) unpack16(raw[slot][u], buf[u], (const T*)nullptr);
+      for (int u = 0; u < U; ++u) unpack16(ring[(st * U + u) * kPyrThreads + threadIdx.x], buf[u], (const T*)nullptr);
       // the U tokens' norm reductions run side by side (independent shuffle chains)
       float nrms[U];
       if (scored) {
@@ -122,14 +140,20 @@ pyramid_score_kernel(const T* __restrict__ xq, const T* __restrict__ xk, const T
         }
       }
     };
-    // two batches per trip so that the buffer index is a compile-time constant
-    load_batch(0, 0);
-    for (int i0 = 0; i0 < ntok; i0 += 2 * U) {
-      if (i0 + U < ntok) load_batch(1, i0 + U);
-      process(0, i0);
-      if (i0 + U >= ntok) break;
-      if (i0 + 2 * U < ntok) load_batch(0, i0 + 2 * U);
-      process(1, i0 + U);
+    // One commit group per batch (empty past the end), so that "batch n has
+    // landed" is "at most NST-1 groups pending" at trip n.  A stage is refilled
+    // only after this thread has reduced the values read from it.
+    const int nb = (ntok + U - 1) / U;
+#pragma unroll
+    for (int n = 0; n < NST; ++n) {
+      if (n < nb) issue(n);
+      pyr_commit();
+    }
+    for (int n = 0; n < nb; ++n) {
+      asm volatile("cp.async.wait_group %0;" ::"n"(NST - 1) : "memory");
+      process(n);
+      if (n + NST < nb) issue(n + NST);
+      pyr_commit();
     }
   }
   if (!scored) return;
@@ -156,7 +180,8 @@ static int launch_pyr(const void* xq, const void* xk, const void* xv, int B, int
   const int S_pool = pyr.total - S;
   int tpc_tot = 0;
   for (int l = 0; l < LV; ++l) tpc_tot += tpc >> (l * shift);
-  const size_t smem = (size_t)H * tpc_tot * sizeof(float);
+  const size_t ring = (size_t)kPyrStages * kPyrU * kPyrThreads * 16;
+  const size_t smem = ring + (size_t)H * tpc_tot * sizeof(float);
   if (smem > 200 * 1024) { set_error("pyramid: H*tpc too large for shared memory"); return LH_ERR_SHAPE; }
   auto kern = pyramid_score_kernel<T, D, LV>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

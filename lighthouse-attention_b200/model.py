@@ -166,8 +166,18 @@ class Block(nn.Module):
         self.feed_forward = FeedForward(args.dim, args.hidden_dim)
 
     def forward(self, x, freqs, cp_info=None):
-        h = x + self.attention(self.attention_norm(x), freqs, cp_info)
-        return h + self.feed_forward(self.ffn_norm(h))
+        h = x + self.attention(_to_compute_dtype(self.attention_norm(x)), freqs, cp_info)
+        return h + self.feed_forward(_to_compute_dtype(self.ffn_norm(h)))
+
+
+def _to_compute_dtype(t):
+    """Under autocast, cast a normalised fp32 activation to the autocast dtype
+    once.  Autocast would otherwise cast it separately for every projection that
+    reads it (wq, wk, wv; w1, w3), with one more conversion per projection in
+    backward.  The projections see the same bf16 values either way."""
+    if t.is_cuda and torch.is_autocast_enabled("cuda"):
+        return t.to(torch.get_autocast_dtype("cuda"))
+    return t
 
 
 class Transformer(nn.Module):

@@ -119,20 +119,29 @@ def run_ours(args, rank, world, local_rank):
         e.record()
         ev.setdefault(name, []).append(e)
 
+    # segment boundaries inside one step: every kernel group of the layer gets
+    # its own pair of events on the launching (current) stream
+    SEG = ["pyramid", "select", "gather", "attn_fwd", "scatter_fwd", "scatter_bwd", "attn_bwd", "unpool_bwd"]
+
     def step(timed):
         # the fused layer of lighthouse_selection._LighthouseLayerFn, instrumented
+        if timed: mark("start")
         pq, pk, pv, sqk, skq = N.pyramid_score(xq, xk, xv, L, p)
+        if timed: mark("pyramid")
         idx, inv = N.select_topk(sqk, skq, L, p, k, S)
+        if timed: mark("select")
         qs, ks, vs = N.gather_selected([xq, xk, xv], [pq, pk, pv], idx)
-        if timed: mark("fwd0")
+        if timed: mark("gather")
         o, lse = N.attn_fwd(qs, ks, vs, scale)
-        if timed: mark("fwd1")
+        if timed: mark("attn_fwd")
         out = N.scatter_fwd(o, inv, S, S, L, p)
+        if timed: mark("scatter_fwd")
         dattn = N.scatter_bwd(dout, idx, S, S, L, p)
-        if timed: mark("bwd0")
+        if timed: mark("scatter_bwd")
         dqs, dks, dvs = N.attn_bwd(qs, ks, vs, o, lse, dattn, scale)
-        if timed: mark("bwd1")
+        if timed: mark("attn_bwd")
         dx = N.unpool_bwd([dqs, dks, dvs], inv, S, L, p)
+        if timed: mark("unpool_bwd")
         return out, dx
 
     for _ in range(args.warmup):
@@ -154,9 +163,40 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             torch.distributed.barrier()
     ms = t0.elapsed_time(t1) / args.steps
-    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ev["fwd0"], ev["fwd1"]))
-    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ev["bwd0"], ev["bwd1"]))
+    seg_ms = {}
+    prev = "start"
+    for name in SEG:
+        seg_ms[name] = statistics.mean(a.elapsed_time(b) for a, b in zip(ev[prev], ev[name]))
+        prev = name
+    fwd_ms, bwd_ms = seg_ms["attn_fwd"], seg_ms["attn_bwd"]
     assert N.device_status() == 0, "an attention kernel left a bounded wait"
+
+    # The reference runs F.scaled_dot_product_attention (cuDNN on sm_100) on
+    # the gathered sequence: time it here on the same q/k/v/dO, same stream.
+    sdpa_fwd_ms = sdpa_bwd_ms = None
+    if not args.no_sdpa:
+        with torch.no_grad():
+            pq, pk, pv, sqk, skq = N.pyramid_score(xq, xk, xv, L, p)
+            idx, inv = N.select_topk(sqk, skq, L, p, k, S)
+            qs, ks, vs = N.gather_selected([xq, xk, xv], [pq, pk, pv], idx)
+            dattn = N.scatter_bwd(dout, idx, S, S, L, p)
+            del pq, pk, pv, sqk, skq, inv
+        qg, kg, vg = (t.detach().requires_grad_(True) for t in (qs, ks, vs))
+        sf, sb = [], []
+        for it in range(args.warmup + min(args.steps, 10)):
+            a0, a1, a2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            a0.record()
+            og = torch.nn.functional.scaled_dot_product_attention(qg, kg, vg, is_causal=True)
+            a1.record()
+            og.backward(dattn)
+            a2.record()
+            if it >= args.warmup:
+                sf.append((a0, a1)); sb.append((a1, a2))
+            qg.grad = kg.grad = vg.grad = None
+        torch.cuda.synchronize()
+        sdpa_fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in sf)
+        sdpa_bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in sb)
+        del qg, kg, vg, og, qs, ks, vs, dattn, idx
 
     # end to end through the public API: pinned host inputs -> device, scalar loss back
     (hq, hk, hv), _ = _inputs("cpu")
@@ -215,36 +255,45 @@ def run_ours(args, rank, world, local_rank):
     per_rank = None
     if world > 1:
         # every rank's figures, so that a slow GPU setting the max shows by itself
-        mine = torch.tensor([ms, e2e_ms, fwd_ms, bwd_ms, float(clocks["sm_mhz"] or 0)], device=dev)
+        mine = torch.tensor([ms, e2e_ms, fwd_ms, bwd_ms, float(clocks["sm_mhz"] or 0)]
+                            + [seg_ms[n] for n in SEG], device=dev)
         allr = torch.empty(world, mine.numel(), device=dev)
         torch.distributed.all_gather_into_tensor(allr, mine)
         per_rank = [{"ms_per_step": r[0], "e2e_ms": r[1], "attn_fwd_ms": r[2], "attn_bwd_ms": r[3], "sm_mhz": r[4]}
                     for r in allr.tolist()]
-        ms, e2e_ms, fwd_ms, bwd_ms = allr[:, :4].max(dim=0).values.tolist()
+        mx = allr.max(dim=0).values.tolist()
+        ms, e2e_ms, fwd_ms, bwd_ms = mx[:4]
+        seg_ms = dict(zip(SEG, mx[5:]))
     if rank != 0:
         return
 
-    P = _sel_len(S, L, p, k) * (_sel_len(S, L, p, k) + 1) / 2
+    S_sel = _sel_len(S, L, p, k)
+    P = S_sel * (S_sel + 1) / 2
     bwd_flops = 10 * B * H * D * P
     fwd_flops = 4 * B * H * D * P
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except OSError:
-        pass
-    peak = peaks.get("bf16_tflops_sustained") or 1400.0
-    peak_src = "measured sustained" if "bf16_tflops_sustained" in peaks else "fallback"
+    pk_ = _peak_for(ms * args.steps * 1e-3)
+    peak = pk_["tflops"]
     achieved = bwd_flops / (bwd_ms * 1e-3) / 1e12
-    traffic = None
-    if (B, S, H, D, L, p, k) == (1, 131072, 8, 128, 3, 4, 2048):
-        # DRAM read + write of attn_bwd_kernel per launch from the committed ncu launch list
-        import re
-        try:
-            txt = open(os.path.join(ROOT, "profiles", "launches_layer_S131072_k2048.md")).read()
-            m = re.search(r"traffic_bytes_per_launch attn_bwd: (\d+)", txt)
-            traffic = int(m.group(1)) if m else None
-        except OSError:
-            pass
+    hbm = pk_["gbs"]
+    # algorithmic bytes of the HBM-bound kernels (per launch)
+    S_tot = sum(S // p ** l for l in range(L))
+    S_pool = S_tot - S
+    row = D * 2
+    hb = {
+        "pyramid": 3 * B * S * H * row + 3 * B * H * S_pool * row + 2 * B * H * S_tot * 4,
+        "select": 2 * B * H * 4 * (S // p ** (L - 1) + 2 * (L - 1) * p * k) + B * H * (S_sel + S_tot) * 4,
+        "gather": 2 * 3 * B * H * S_sel * row,
+        "scatter_fwd": B * H * S * row + B * H * S_sel * row,
+        "scatter_bwd": B * H * S * row + B * H * S_sel * row,
+        "unpool_bwd": 3 * B * S * H * row + 3 * B * H * S_sel * row,
+    }
+    hbm_kernels = {n: {"ms": seg_ms[n], "bytes": hb[n], "gbs": hb[n] / (seg_ms[n] * 1e-3) / 1e9,
+                       "frac": hb[n] / (seg_ms[n] * 1e-3) / 1e9 / hbm} for n in hb}
+    pss_bytes = hb["pyramid"] + hb["select"]
+    pss_ms = seg_ms["pyramid"] + seg_ms["select"]
+    hbm_kernels["pool_score_select"] = {"ms": pss_ms, "bytes": pss_bytes, "gbs": pss_bytes / (pss_ms * 1e-3) / 1e9,
+                                        "frac": pss_bytes / (pss_ms * 1e-3) / 1e9 / hbm}
+    attn_tf = (fwd_flops + bwd_flops) / ((fwd_ms + bwd_ms) * 1e-3) / 1e12
     tokens = B * S * world
     line = {
         "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
@@ -253,21 +302,32 @@ def run_ours(args, rank, world, local_rank):
         "config": _config({"parallelism": f"replicas x{world}"}),
         "roofline": {"kernel": "attn_bwd (prep + tcgen05 main + post)", "bound": "tensor",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                     "peak_source": peak_src, "traffic": traffic, "traffic_unit": "bytes per launch (ncu)",
-                     "flops_per_launch": bwd_flops, "ms_per_launch": bwd_ms},
+                     "peak_source": pk_["tf_src"], "traffic": None,
+                     "traffic_note": "not measured in this run (ncu DRAM counters of a small-shape capture "
+                                     "are summarised under profiles/)",
+                     "flops_per_launch": bwd_flops, "ms_per_launch": bwd_ms,
+                     "attn_fwd": {"achieved": fwd_flops / (fwd_ms * 1e-3) / 1e12,
+                                  "frac": fwd_flops / (fwd_ms * 1e-3) / 1e12 / peak, "ms_per_launch": fwd_ms,
+                                  "flops_per_launch": fwd_flops},
+                     "attn_fwd_bwd": {"achieved": attn_tf, "frac": attn_tf / peak},
+                     "hbm_peak_gbs": hbm, "hbm_peak_source": pk_["gbs_src"], "hbm_kernels": hbm_kernels},
         "kernels": {"attn_fwd_ms": fwd_ms, "attn_fwd_tflops": fwd_flops / (fwd_ms * 1e-3) / 1e12,
                     "attn_bwd_ms": bwd_ms, "attn_bwd_tflops": achieved,
-                    "rest_ms": ms - fwd_ms - bwd_ms},
+                    "rest_ms": ms - fwd_ms - bwd_ms, "segments_ms": seg_ms,
+                    "cudnn_fwd_ms": sdpa_fwd_ms, "cudnn_bwd_ms": sdpa_bwd_ms,
+                    "cudnn_note": "torch scaled_dot_product_attention(is_causal=True), the reference's attention "
+                                  "call, on the identical gathered q/k/v and scattered dO, same run"},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms, "api": "lighthouse_attention",
                 "input_pipeline": "step i+1 host->device copy on a second stream during step i"},
         "gpu_launches": 10 * args.steps,
+        "timed_region_s": ms * args.steps * 1e-3,
         "clocks": clocks,
     }
     if per_rank:
         line["per_rank"] = per_rank
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_sample(steps=2, warmup=1)["cpu_baseline"]   # warm, as the reference arm
+        line["cpu_baseline"] = cpu_sample(steps=1, warmup=1)["cpu_baseline"]   # warm, as the reference arm
     print(json.dumps(line), flush=True)
 
 
@@ -437,15 +497,27 @@ def run_sweep(args, rank, world, local_rank):
 
 
 # ----------------------------------------------------------------------------- GLA scorer workload
-def _peaks():
-    """Dense bf16 peak for a kernel timed on its own: the measured burst figure."""
+def _peak_for(timed_s: float):
+    """Roofline denominators from MEASURED_PEAKS.json.  The burst bf16 figure
+    applies to a timed region shorter than 2 s; the sustained (power-capped)
+    one to longer regions."""
     try:
         m = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except OSError:
         m = {}
-    if "bf16_tflops" in m:
-        return {"tflops": m["bf16_tflops"], "tf_src": "measured burst"}
-    return {"tflops": 1590.0, "tf_src": "fallback"}
+    if timed_s >= 2.0 and "bf16_tflops_sustained" in m:
+        tf, src = m["bf16_tflops_sustained"], "measured sustained (timed region >= 2 s)"
+    elif "bf16_tflops" in m:
+        tf, src = m["bf16_tflops"], "measured burst (timed region < 2 s)"
+    else:
+        tf, src = (1400.0, "fallback sustained") if timed_s >= 2.0 else (1590.0, "fallback burst")
+    gbs, gsrc = (m["hbm_gbs"], "measured") if "hbm_gbs" in m else (6650.0, "fallback")
+    return {"tflops": tf, "tf_src": src, "gbs": gbs, "gbs_src": gsrc}
+
+
+def _peaks():
+    """Dense bf16 peak for a kernel timed on its own: the measured burst figure."""
+    return _peak_for(0.0)
 
 
 def run_scorer_gla(args, rank, world, local_rank):
@@ -500,8 +572,12 @@ def run_scorer_gla(args, rank, world, local_rank):
     assert lh._native.device_status() == 0
     if world > 1:
         t = torch.tensor([ms, kms, e2e_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, kms, e2e_ms = t.tolist()
+        allr = torch.empty(world, 3, device=dev)
+        torch.distributed.all_gather_into_tensor(allr, t)
+        per_rank = [{"ms_per_step": r[0], "kernel_ms": r[1], "e2e_ms": r[2]} for r in allr.tolist()]
+        ms, kms, e2e_ms = allr.max(dim=0).values.tolist()
+    else:
+        per_rank = None
     if rank != 0:
         return
     # algorithmic FLOPs: the recurrence's state update k v^T and read-out q S, 2 D^2 multiply-adds
@@ -523,10 +599,8 @@ def run_scorer_gla(args, rank, world, local_rank):
                 "h2d_bytes_per_step": sum(h.numel() * h.element_size() for h in host), "d2h_bytes_per_step": 4,
                 "ms_per_step": e2e_ms, "api": "DilatedLighthouseGLAScorer.scores"},
         "gpu_launches": 3 * args.steps,          # scorer: GLA + pyramid; kernel leg: GLA
-        "clocks": clocks,
+        "clocks": clk.summary(),
     }
-    if per_rank:
-        line["per_rank"] = per_rank
     if world == 1 and not args.no_cpu_baseline:
         # the oracle (fp32 recurrence, ATen on the host threads) on the first 8192 tokens;
         # its cost is linear in the sequence length, so tokens/s carries over
@@ -540,16 +614,19 @@ def run_scorer_gla(args, rank, world, local_rank):
                                 "kind": "port", "dtype": "f32",
                                 "sample": f"first {n} of {S} tokens, all heads, both passes + pyramid; oracle "
                                           "recurrence (fla's published simple-GLA definition)"}
+    if per_rank:
+        line["per_rank"] = per_rank
     print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------------------------------------- CPU arm
 def cpu_sample(steps: int, warmup: int):
-    """The reference path on the host cores, one head of the workload per step."""
+    """The reference path on the host cores: the whole layer (all heads)
+    forward + backward per step, fp32, on all host threads."""
     from oracle import oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
     B, S, H, D, L, p, k = (CFG[x] for x in ("B", "S", "H", "D", "L", "p", "k"))
-    (xq, xk, xv), dout = _inputs("cpu", torch.float32, heads=[0])
+    (xq, xk, xv), dout = _inputs("cpu", torch.float32)
 
     def one():
         xs = [t.clone().requires_grad_(True) for t in (xq, xk, xv)]
@@ -562,11 +639,11 @@ def cpu_sample(steps: int, warmup: int):
     for _ in range(steps):
         one()
     dt = (time.perf_counter() - t0) / steps
-    value = (B * S / H) / dt          # one of H heads per step
+    value = (B * S) / dt
     return {"value": value, "sec_per_step": dt, "cpu_baseline": {
         "value": value, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
         "dtype": "f32",
-        "sample": f"1 of {H} heads of the S={S} layer fwd+bwd per step, tokens/s scaled by 1/{H}; "
+        "sample": f"the whole S={S} layer (all {H} heads) fwd+bwd, {steps} timed step(s) after {warmup} warm-up; "
                   "oracle restatement (ATen scorer, C selection, gather, CPU SDPA, index_add scatter)"}}
 
 
@@ -577,7 +654,7 @@ def run_reference(args, rank):
     warm = min(args.warmup, 1)
     r = cpu_sample(steps, warm)
     line = {"metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
-            "warmup": warm, "ms_per_step": r["sec_per_step"] * 1e3 * CFG["H"], "higher_is_better": True,
+            "warmup": warm, "ms_per_step": r["sec_per_step"] * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
             "config": _config({"parallelism": "cpu"}), "impl": "reference",
             "cpu_baseline": r["cpu_baseline"],
@@ -592,6 +669,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sdpa", action="store_true", help="skip the same-run cuDNN SDPA comparison")
     ap.add_argument("--workload", default="layer", choices=["layer", "model", "model_cp", "scorer_gla", "sweep"],
                     help="layer: BASELINE config 3 (default); model: config 4, the 270M training step; "
                          "model_cp: config 5, one sequence context-parallel over the N ranks; "

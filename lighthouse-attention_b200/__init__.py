@@ -1,8 +1,8 @@
 """lighthouse_b200 — B200 (sm_100a) implementation of Lighthouse selection attention.
 
 The directory is named ``lighthouse-attention_b200``; it is imported under the
-package name ``lighthouse_b200`` (see ``load_package`` in __graft_entry__.py
-or INTEGRATION.md).  Modules:
+package name ``lighthouse_b200`` (``load_package`` in __graft_entry__.py does
+that with importlib).  Modules:
 
   lighthouse_selection       drop-in for the reference module of the same name
   lighthouse_selection_cuda  drop-in for the reference module of the same name

@@ -23,9 +23,9 @@ import math
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from . import _native
+from ._native import LighthouseShapeError
 from .library import ops as _ops
 from .lighthouse_selection_cuda import (LighthouseSelectionQkKqChunkedTopkNvrtc,  # noqa: F401
                                         compute_output_indices_selection)
@@ -88,12 +88,15 @@ class DialatedLighthouseNormScorerCP(DialatedLighthouseNormScorer):
 
 
 def _causal_attention(q, k, v):
-    """(B, H, S, D) causal attention: this package's tcgen05 kernel for bf16 with
-    D = 128, scaled_dot_product_attention otherwise."""
-    if q.dtype == torch.bfloat16 and q.shape[-1] == 128 and q.is_cuda:
-        o, _ = _ops.attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), 1.0 / math.sqrt(q.shape[-1]))
-        return o
-    return F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    """(B, H, S, D) causal attention on this package's tcgen05 kernel.  It is
+    defined for bf16 CUDA tensors with D = 128 only; anything else raises (a
+    caller that wants another attention passes it as ``attention=``)."""
+    if not (q.dtype == torch.bfloat16 and q.shape[-1] == 128 and q.is_cuda):
+        raise LighthouseShapeError(
+            "dilated scorer: the default attention needs bf16 CUDA tensors with head_dim 128 "
+            f"(got {q.dtype}, head_dim {q.shape[-1]}, device {q.device}); pass attention= for other inputs")
+    o, _ = _ops.attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), 1.0 / math.sqrt(q.shape[-1]))
+    return o
 
 
 class DilatedLighthouseScorer(nn.Module):

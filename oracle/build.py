@@ -30,7 +30,9 @@ import subprocess
 
 HERE = pathlib.Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-REFERENCE_CU = pathlib.Path("/root/reference/src/lighthouse_selection_cuda.py")
+# The reference tree: LH_REFERENCE_ROOT, else the build container's mount point.
+REFERENCE_ROOT = pathlib.Path(os.environ.get("LH_REFERENCE_ROOT", "/root/reference"))
+REFERENCE_CU = REFERENCE_ROOT / "src" / "lighthouse_selection_cuda.py"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 POOLING_FACTORS = (2, 4, 8)
 

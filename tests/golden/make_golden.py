@@ -46,7 +46,8 @@ sys.path.insert(0, str(HERE))
 from inputs import (GLA_CASES, SCORER_CASES, SELECT_CASES, SCATTER_CASES, LAYER_CASES, checksum, make_gate,
                     make_scores, make_qkv)  # noqa: E402
 
-REF = pathlib.Path("/root/reference/src")
+# The reference tree: LH_REFERENCE_ROOT, else the build container's mount point.
+REF = pathlib.Path(os.environ.get("LH_REFERENCE_ROOT", "/root/reference")) / "src"
 
 
 def _load(name, path):

@@ -33,3 +33,26 @@ def test_headline_workload_is_defined(O):
     c = b.CFG
     assert O.shape_defined(c["S"], c["L"], c["p"], c["k"])
     assert b._sel_len(c["S"], c["L"], c["p"], c["k"]) == 24576
+
+
+def test_bench_functions_read_no_undefined_globals():
+    """Every global name a bench.py function reads is defined at module level or
+    is a builtin (a NameError in a rarely run --workload would otherwise only
+    show on the GPU box)."""
+    import builtins
+    import symtable
+    src = (ROOT / "bench.py").read_text()
+    top = symtable.symtable(src, "bench.py", "exec")
+    defined = set(top.get_identifiers()) | set(dir(builtins))
+    missing = []
+
+    def walk(tab):
+        for child in tab.get_children():
+            if child.get_type() == "function":
+                for sym in child.get_symbols():
+                    if sym.is_global() and sym.is_referenced() and sym.get_name() not in defined:
+                        missing.append((child.get_name(), sym.get_name()))
+            walk(child)
+
+    walk(top)
+    assert not missing, missing

@@ -87,3 +87,53 @@ def test_attn_bwd_vs_fp32_reference(lh, cuda, case):
     _check(dq, qr.grad, "dQ")
     _check(dk, kr.grad, "dK")
     _check(dv, vr.grad, "dV")
+
+
+def _ref_fwd_bwd_chunked(q, k, v, do, scale, chunk=2048):
+    """fp32 causal attention forward + backward for one (b, h) slice, in query
+    chunks so that no S x S matrix is held at once:
+    P = softmax(scale QK^T + mask), O = PV, Delta = rowsum(dO * O),
+    dS = P * (dO V^T - Delta), dQ = scale dS K, dK = scale dS^T Q, dV = P^T dO."""
+    qf, kf, vf, dof = q.float(), k.float(), v.float(), do.float()
+    S = qf.shape[0]
+    o = torch.empty_like(qf)
+    dq = torch.empty_like(qf)
+    dk = torch.zeros_like(kf)
+    dv = torch.zeros_like(vf)
+    kpos = torch.arange(S, device=q.device)[None, :]
+    for c0 in range(0, S, chunk):
+        c1 = min(S, c0 + chunk)
+        qpos = torch.arange(c0, c1, device=q.device)[:, None]
+        s = (qf[c0:c1] @ kf[:c1].T) * scale
+        s = s.masked_fill(kpos[:, :c1] > qpos, float("-inf"))
+        p = torch.softmax(s, dim=-1)
+        del s
+        o[c0:c1] = p @ vf[:c1]
+        delta = (dof[c0:c1] * o[c0:c1]).sum(-1, keepdim=True)
+        ds = p * (dof[c0:c1] @ vf[:c1].T - delta)
+        dv[:c1] += p.T @ dof[c0:c1]
+        del p
+        dq[c0:c1] = (ds @ kf[:c1]) * scale
+        dk[:c1] += (ds.T @ qf[c0:c1]) * scale
+    return o, dq, dk, dv
+
+
+@pytest.mark.parametrize("S_sel", [20480, 24576])
+def test_attn_fwd_bwd_at_product_selected_lengths(lh, cuda, S_sel):
+    """The selected lengths the layer runs at BASELINE configs 2 (S=65536,
+    k=2048: S_sel=20480) and 3 (S=131072, k=2048: S_sel=24576), all 8 heads in
+    one launch (the grid and the fp32 dQ accumulation as in the product),
+    each head checked against the chunked fp32 reference."""
+    B, H = 1, 8
+    q, k, v, do = _inputs(B, H, S_sel, S_sel, 5, cuda)
+    scale = 1 / math.sqrt(128)
+    o, lse = lh._native.attn_fwd(q, k, v, scale)
+    dq, dk, dv = lh._native.attn_bwd(q, k, v, o, lse, do, scale)
+    torch.cuda.synchronize()
+    assert lh._native.device_status() == 0
+    for h in range(H):
+        ro, rdq, rdk, rdv = _ref_fwd_bwd_chunked(q[0, h], k[0, h], v[0, h], do[0, h], scale)
+        _check(o[0, h], ro, f"O head {h}")
+        _check(dq[0, h], rdq, f"dQ head {h}")
+        _check(dk[0, h], rdk, f"dK head {h}")
+        _check(dv[0, h], rdv, f"dV head {h}")

@@ -134,3 +134,33 @@ def test_dilated_scorer_and_layer(lh, O, cuda, shape):
         m, r = _err(a.grad.cpu(), b.grad)
         assert m <= 2e-2 and r <= 1e-2, f"d{n} max-abs {m:.3e} rel {r:.3e}"
     assert lh._native.device_status() == 0
+
+
+def test_lighthouse_local_baseline_config2_vs_oracle(lh, O, cuda):
+    """BASELINE config 2 (B=1, S=65536, H=8, D=128, L=3, p=4, k=2048) through the
+    module API, forward + backward, all eight heads on the GPU; heads 0 and 5
+    checked against the fp32 oracle layer (run on the GPU, math SDPA) on the
+    kernels' own selection."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    B, S, H, D, L, p, k = 1, 65536, 8, 128, 3, 4, 2048
+    xq, xk, xv = make_qkv(B, S, H, D, torch.bfloat16, 0)
+    g = torch.Generator().manual_seed(1)
+    dout = torch.randn(B, H, S, D, generator=g).to(torch.bfloat16)
+    layer = lh.LighthouseLocal(None, lh.DialatedLighthouseNormScorer(p, L), num_levels=L, pooling_factor=p, topk=k)
+    xs = [t.to(cuda).requires_grad_(True) for t in (xq, xk, xv)]
+    out = layer(*xs)
+    out.backward(dout.to(cuda))
+    _, _, _, sqk, skq = lh._native.pyramid_score(*[t.detach() for t in xs], L, p)
+    idx = lh._native.select_topk(sqk, skq, L, p, k, S)[0]
+    assert idx.shape == (B, H, O.sel_len(S, L, p, k))
+    heads = [0, 5]
+    xr = [t[:, :, heads].float().to(cuda).requires_grad_(True) for t in (xq, xk, xv)]
+    with sdpa_kernel(SDPBackend.MATH):
+        ref, _ = O.lighthouse_local(*xr, L, p, k, indices=idx[:, heads])
+        ref.backward(dout[:, heads].float().to(cuda))
+    m, r = _err(out[:, heads].detach(), ref.detach())
+    assert m <= 2e-2 and r <= 1e-2, f"out max-abs {m:.3e} rel {r:.3e}"
+    for a, b, n in zip(xs, xr, "qkv"):
+        m, r = _err(a.grad[:, :, heads], b.grad)
+        assert m <= 2e-2 and r <= 1e-2, f"d{n} max-abs {m:.3e} rel {r:.3e}"
+    assert lh._native.device_status() == 0

@@ -65,3 +65,58 @@ def test_fused_rope_matches_complex_formulation(lh, cuda, dtype):
     eq, ek = torch.autograd.grad((rq, rk), (xq, xk), (gq, gk))
     for a, b in ((dq, eq), (dk, ek)):
         assert ((a.float() - b.float()).abs() <= ulp * b.float().abs() + 1e-5).all()
+
+
+@pytest.mark.gpu
+def test_model_logits_and_grads_match_oracle_layers(lh, O, cuda, monkeypatch):
+    """A 4-layer model (3 Lighthouse layers) under the training autocast: logits
+    and every parameter gradient match the same model (same weights, same
+    tokens) whose Lighthouse layers run the fp32 oracle layer (SEL:789-825 on
+    the GPU, math SDPA) on the kernels' own selection.  Only the Lighthouse
+    attention differs between the two runs, so the north-star tolerance for
+    attention outputs and gradients applies to what reaches the logits and the
+    weights through it."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    from lighthouse_b200 import model as M
+    args = M.ModelArgs(dim=256, n_layers=4, n_heads=2, n_kv_heads=2, hidden_dim=384, max_seq_len=4096,
+                       lighthouse_topk=256, lighthouse_full_attn_layers=[0])
+    g = torch.Generator().manual_seed(5)
+    tokens = torch.randint(0, 256, (1, 4097), generator=g).to(cuda)
+
+    def run():
+        torch.manual_seed(0)
+        m = M.Transformer(args).to(cuda)
+        m.init_weights(0)
+        inputs, labels = tokens[:, :-1], tokens[:, 1:]
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = m(inputs)
+        loss = torch.nn.functional.cross_entropy(logits.float().reshape(-1, 256), labels.reshape(-1))
+        loss.backward()
+        return logits.detach().float(), {n: p.grad.detach().float() for n, p in m.named_parameters()}
+
+    logits, grads = run()
+
+    def oracle_layer(xq, xk, xv, L, p, k):
+        with torch.no_grad():
+            _, _, _, sqk, skq = lh._native.pyramid_score(xq.detach().contiguous(), xk.detach().contiguous(),
+                                                         xv.detach().contiguous(), L, p)
+            idx = lh._native.select_topk(sqk, skq, L, p, k, xq.shape[1])[0]
+        with torch.autocast("cuda", enabled=False), sdpa_kernel(SDPBackend.MATH):
+            out, _ = O.lighthouse_local(xq.float(), xk.float(), xv.float(), L, p, k, indices=idx)
+        return out.to(xq.dtype)
+
+    monkeypatch.setattr(M, "lighthouse_attention", oracle_layer)
+    ref_logits, ref_grads = run()
+
+    def rel(a, b):
+        return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+    r = rel(logits, ref_logits)
+    assert r <= 1e-2, f"logits rel-L2 {r:.3e}"
+    assert (logits - ref_logits).abs().max().item() <= 2e-2
+    flat = torch.cat([grads[n].reshape(-1) for n in grads])
+    ref_flat = torch.cat([ref_grads[n].reshape(-1) for n in grads])
+    assert rel(flat, ref_flat) <= 1e-2, f"all-parameter gradient rel-L2 {rel(flat, ref_flat):.3e}"
+    worst = max(grads, key=lambda n: rel(grads[n], ref_grads[n]))
+    assert rel(grads[worst], ref_grads[worst]) <= 3e-2, f"{worst}: rel-L2 {rel(grads[worst], ref_grads[worst]):.3e}"
+    assert lh._native.device_status() == 0

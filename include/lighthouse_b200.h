@@ -110,6 +110,17 @@ int lh_gather_selected(const void* q_raw, const void* k_raw, const void* v_raw,
 int lh_attn_fwd(const void* q, const void* k, const void* v, int B, int H, int S_q, int S_kv,
                 int q_off, int D, float scale, void* o, float* lse, void* stream);
 
+/* Log-sum-exp merge of two partial attentions of the same query rows over
+ * disjoint key sets: the per-block results of the context-parallel attention
+ * (SEL:1044 under torch's ring attention, whose merge is
+ * torch/distributed/tensor/experimental/_context_parallel/_attention.py:71-77
+ * and the ring loop at :380-470), here the local diagonal chunk and the
+ * all-gathered earlier chunks.
+ *   o1, o2 (rows, D) bf16; lse1, lse2 (rows) fp32 natural-log; D == 128
+ *   o (rows, D) bf16, lse (rows) fp32 out (may alias o1 / lse1) */
+int lh_attn_merge(const void* o1, const float* lse1, const void* o2, const float* lse2, long long rows,
+                  int D, void* o, float* lse, void* stream);
+
 /* Bytes of workspace lh_attn_bwd needs. */
 size_t lh_attn_bwd_workspace_size(int B, int H, int S_q, int S_kv, int D);
 

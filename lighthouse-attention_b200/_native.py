@@ -38,6 +38,7 @@ _SIGS = {
     "lh_gather_selected": (ctypes.c_int, [_VP] * 6 + [ctypes.c_int] * 6 + [_VP, ctypes.c_int] + [_VP] * 4),
     "lh_attn_fwd": (ctypes.c_int, [_VP] * 3 + [ctypes.c_int] * 6 + [ctypes.c_float, _VP, _VP, _VP]),
     "lh_attn_bwd_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 5),
+    "lh_attn_merge": (ctypes.c_int, [_VP] * 4 + [ctypes.c_longlong, ctypes.c_int, _VP, _VP, _VP]),
     "lh_attn_bwd": (ctypes.c_int, [_VP] * 6 + [ctypes.c_int] * 6 + [ctypes.c_float] + [_VP] * 4
                     + [ctypes.c_size_t, _VP]),
     "lh_attn_bwd_noalloc": (ctypes.c_int, [_VP] * 6 + [ctypes.c_int] * 6 + [ctypes.c_float] + [_VP] * 4),
@@ -184,6 +185,20 @@ def attn_fwd(q, k, v, scale: float, q_off: int = 0):
     lse = torch.empty(B, H, S_q, dtype=torch.float32, device=q.device)
     _check(load().lh_attn_fwd(_ptr(q), _ptr(k), _ptr(v), B, H, S_q, S_kv, q_off, D, scale, _ptr(o), _ptr(lse),
                               _stream()))
+    return o, lse
+
+
+def attn_merge(o1, lse1, o2, lse2):
+    """Log-sum-exp merge of two partial attentions of the same queries over
+    disjoint key sets: (o, lse), o bf16 (..., D), lse fp32 (...)."""
+    o1, o2 = _attn_operands(o1, o2)
+    lse1, lse2 = lse1.float().contiguous(), lse2.float().contiguous()
+    if o1.shape != o2.shape or lse1.shape != o1.shape[:-1] or lse2.shape != lse1.shape:
+        raise LighthouseShapeError("attn_merge: o1/o2 and lse1/lse2 must agree")
+    o = torch.empty_like(o1)
+    lse = torch.empty_like(lse1)
+    _check(load().lh_attn_merge(_ptr(o1), _ptr(lse1), _ptr(o2), _ptr(lse2), lse1.numel(), o1.shape[-1], _ptr(o),
+                                _ptr(lse), _stream()))
     return o, lse
 
 

@@ -19,8 +19,9 @@
 //             also into shared memory;
 //               dV_j += P^T_h dO_h            (TS, TMEM cols 256..383)
 //               dK_j += dS^T_h Q_h            (TS, TMEM cols 384..511)
-//               dQ_i^T = K_j^T dS_i^T         (SS, both MN-major; TMEM cols 128..255)
-//             a drain warpgroup reads dQ_i^T (TMEM lane = head dimension) and
+//               dQ_h^T = K_j^T dS_h^T         (SS, both MN-major, N = 64, issued per
+//                                              half into the dP^T_h columns 128 + 64h..)
+//             a drain warpgroup reads dQ_h^T (TMEM lane = head dimension) and
 //             adds it into the fp32 dQacc with coalesced red.global.add: no
 //             shared-memory stage, so shared-memory bandwidth (which the SS
 //             MMAs saturate) is left to the MMAs and the Q / dO refills, and the
@@ -56,7 +57,8 @@ constexpr int kStages = 2;                 // Q_i / dO_i buffers
 }  // namespace bwd
 
 struct BwdSmem {
-  uint64_t kv_full, dq_ready, mma_done;
+  uint64_t kv_full, mma_done;
+  uint64_t dq_ready[2];                                          // dQ^T of query half h complete
   uint64_t dq_free[2];                                           // dQ^T query columns [64h, 64h+64) read
   uint64_t q_full[bwd::kStages][2], q_empty[bwd::kStages][2];   // per stage and 64-query half
   uint64_t s_ready[2], p_ready[2];                               // per 64-query half
@@ -68,9 +70,6 @@ struct BwdSmem {
 static_assert(offsetof(BwdSmem, lse2) % 16 == 0 && offsetof(BwdSmem, delta) % 16 == 0, "float4 reads");
 static_assert((3 + 2 * bwd::kStages) * bwd::kTileBytes + sizeof(BwdSmem) <= 232448, "shared memory per CTA");
 
-__device__ __forceinline__ void named_bar_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -118,9 +117,9 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   if (threadIdx.x == 0) {
     mbar_init(&sm->kv_full, 1);
-    mbar_init(&sm->dq_ready, 1);
     mbar_init(&sm->mma_done, 1);
     for (int h = 0; h < 2; ++h) {
+      mbar_init(&sm->dq_ready[h], 1);
       for (int s = 0; s < kStages; ++s) {
         mbar_init(&sm->q_full[s][h], 1);
         mbar_init(&sm->q_empty[s][h], 1);
@@ -186,7 +185,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       // covered by a barrier below.
       constexpr uint32_t id_s = idesc_bf16_f32(kTile, 64, false, false);     // S^T / dP^T halves: N = 64 queries
       constexpr uint32_t id_kmn = idesc_bf16_f32(kTile, kD, false, true);    // A K-major (TMEM), B MN-major
-      constexpr uint32_t id_mnmn = idesc_bf16_f32(kD, kTile, true, true);    // dQ^T: A MN-major, B MN-major
+      constexpr uint32_t id_mnmn = idesc_bf16_f32(kD, 64, true, true);       // dQ^T half: A MN-major, B MN-major
       // Descriptors are a per-operand base plus a constant offset (the start
       // address field holds addr >> 4 in its low 14 bits and every shared
       // address is below 256 KB, so the add cannot carry out of the field).
@@ -247,10 +246,13 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           }
         }
       } else {
-        // dV += P^T_h dO_h and dK += dS^T_h Q_h with A operands from TMEM:
-        // compute warp w of a quadrant leaves the bf16 pairs of its 16 queries
-        // of half h at columns [64h + 16w, +8) (P^T) and [64h + 16w + 8, +8)
-        // (dS^T).  dQ_i^T = K^T dS^T goes first after the second half.
+        // Per 64-query half h: dQ_h^T = K^T dS^T_h (into the dP^T_h columns,
+        // which the compute warps have read), then dV += P^T_h dO_h and
+        // dK += dS^T_h Q_h with A operands from TMEM: compute warp w of a
+        // quadrant leaves the bf16 pairs of its 16 queries of half h at columns
+        // [64h + 16w, +8) (P^T) and [64h + 16w + 8, +8) (dS^T).  Issuing dQ per
+        // half lets the drain of half h, and with it the next tile's dP^T_h,
+        // proceed while the compute warps work on the other half.
         const uint32_t aK = smem_u32(sK), adS = smem_u32(sdS);
         for (int t = 0; t < n_it && ok; ++t) {
           const int st = t % kStages;
@@ -259,13 +261,13 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             ok = wait(&sm->p_ready[h], t & 1);
             if (!ok) break;
             if (lane == 0) {
-              if (h == 1) {
+              {
+                const uint64_t da = mdesc(aK), db = mdesc(adS + h * kBox);   // dS^T queries of half h: box h
 #pragma unroll
-                for (int kk = 0; kk < kTile / 16; ++kk) {    // dQ_i^T = K^T dS^T   (K = key rows)
-                  const uint64_t da = mdesc(aK), db = mdesc(adS);
-                  mma_ss(tbase + kColDP, da + ((kk * 2048) >> 4), db + ((kk * 2048) >> 4), id_mnmn, kk > 0);
-                }
-                mma_commit(&sm->dq_ready);
+                for (int kk = 0; kk < kTile / 16; ++kk)    // K = 16 key rows per step
+                  mma_ss(tbase + kColDP + h * 64, da + ((kk * 2048) >> 4), db + ((kk * 2048) >> 4), id_mnmn,
+                         kk > 0);
+                mma_commit(&sm->dq_ready[h]);
               }
               const uint64_t dq = mdesc(smem_u32(sQ + st * kTileBytes) + h * 4 * 2048);
               const uint64_t ddo = mdesc(smem_u32(sdO + st * kTileBytes) + h * 4 * 2048);
@@ -295,13 +297,13 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     bool ok = true;
     for (int t = 0; t < n_it && ok; ++t) {
       const int i = i0 + t;
-      ok = mbar_wait(&sm->dq_ready, t & 1, abort);
-      if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
-      tc_fence_after();
       float* dst = dQacc + ((size_t)bh * S_q + (size_t)i * kTile) * kD + d;
       const int rows = S_q - i * kTile < kTile ? S_q - i * kTile : kTile;
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {               // query rows [64h, 64h+64)
+        ok = mbar_wait(&sm->dq_ready[h], t & 1, abort);
+        if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+        tc_fence_after();
         uint32_t v[2][32];
         tmem_ld32(lane_base + kColDP + h * 64, v[0]);
         tmem_ld32(lane_base + kColDP + h * 64 + 32, v[1]);

@@ -60,6 +60,7 @@ int unpool_bwd(const void*, const void*, const void*, const int32_t*, int, int, 
 int attn_fwd(const void*, const void*, const void*, int, int, int, int, int, int, float, void*, float*,
              cudaStream_t);
 size_t attn_bwd_workspace_size(int, int, int, int, int);
+int attn_merge(const void*, const float*, const void*, const float*, long long, int, void*, float*, cudaStream_t);
 int attn_status(int reset);
 int rope_apply(const void*, const void*, void*, void*, const float*, int, int, int, int, int, int, cudaStream_t);
 int simple_gla_fwd(const void*, const void*, void*, const void*, const void*, void*, const void*, const float*, int, int,
@@ -137,6 +138,17 @@ int lh_gather_selected(const void* qr, const void* kr, const void* vr, const voi
              "gather: output given without its source tensors");
   LH_ARCH();
   return gather_selected(qr, kr, vr, qp, kp, vp, dtype, B, S, H, D, S_pool, indices, S_sel, qs, ks, vs, S_(stream));
+}
+
+int lh_attn_merge(const void* o1, const float* lse1, const void* o2, const float* lse2, long long rows, int D,
+                  void* o, float* lse, void* stream) {
+  g_err[0] = 0;
+  LH_REQUIRE(o1 && lse1 && o2 && lse2 && o && lse, LH_ERR_ARG, "attn_merge: null pointer");
+  LH_REQUIRE(D == 128, LH_ERR_SHAPE, "attn_merge: head dim must be 128, got %d", D);
+  LH_REQUIRE(rows > 0, LH_ERR_SHAPE, "attn_merge: empty shape");
+  LH_REQUIRE((((uintptr_t)o1 | (uintptr_t)o2 | (uintptr_t)o) & 7) == 0, LH_ERR_ARG, "attn_merge: rows must be 8-byte aligned");
+  LH_ARCH();
+  return attn_merge(o1, lse1, o2, lse2, rows, D, o, lse, S_(stream));
 }
 
 int lh_attn_fwd(const void* q, const void* k, const void* v, int B, int H, int S_q, int S_kv, int q_off, int D,

@@ -50,11 +50,27 @@ def attn_fwd(q, k, v, scale, q_off=0):
 
 
 def attn_bwd(q, k, v, o, lse, do, scale, q_off=0):
-    with torch.enable_grad():
-        qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
-        out, _ = _attn(qr, kr, vr, q_off)
-        out.backward(do.float())
-    return qr.grad.to(q.dtype), kr.grad.to(k.dtype), vr.grad.to(v.dtype)
+    """Backward of one key block given the row statistics of the whole
+    attention (o, lse), as the product kernel computes it:
+    P = exp(scale QK^T - lse), Delta = rowsum(dO o), dS = P (dO V^T - Delta)."""
+    qf, kf, vf, of, dof = (t.float() for t in (q, k, v, o, do))
+    S_q, S_kv = q.shape[2], k.shape[2]
+    s = qf @ kf.transpose(-1, -2) * scale
+    pq = torch.arange(S_q)[:, None] + q_off
+    pk = torch.arange(S_kv)[None, :]
+    p = torch.exp(s - lse.float()[..., None]).masked_fill(pk > pq, 0.0)
+    delta = (dof * of).sum(-1, keepdim=True)
+    ds = p * (dof @ vf.transpose(-1, -2) - delta)
+    dq = ds @ kf * scale
+    dk = ds.transpose(-1, -2) @ qf * scale
+    dv = p.transpose(-1, -2) @ dof
+    return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
+
+
+def attn_merge(o1, lse1, o2, lse2):
+    lse = torch.logaddexp(lse1, lse2)
+    o = torch.exp(lse1 - lse)[..., None] * o1.float() + torch.exp(lse2 - lse)[..., None] * o2.float()
+    return o.to(o1.dtype), lse
 
 
 def scatter_fwd(attn, inv, N, N_total, L, p):

@@ -344,18 +344,29 @@ def run_model(args, rank, world, local_rank, cp=False):
     from lighthouse_b200 import model as M
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    seq = args.seq_len or 65536
-    margs = M.ModelArgs(max_seq_len=seq)
+    # config 5 (CP): seq 262144 with k=1536 is outside the reference's defined
+    # domain (its selection writes holes there); its defined twin is seq 196608
+    seq = args.seq_len or (196608 if cp else 65536)
+    margs = M.ModelArgs(max_seq_len=seq, lighthouse_topk=args.topk or (1536 if cp else 2048))
     torch.manual_seed(0)
     model = M.Transformer(margs).to(dev)
     model.init_weights(0)
+    cpn = min(args.cp or 2, world) if cp else 1       # context-parallel group size (config 5: 2)
+    if cp and world % cpn:
+        raise SystemExit(f"--cp {cpn} must divide the {world} ranks")
+    dp = world // cpn
     if cp and world > 1:
-        model.set_cp_info(rank, world, torch.distributed.new_group(list(range(world))))
+        # ranks [g*cpn, (g+1)*cpn) train one sequence together; every rank
+        # creates every group (new_group is collective over the world)
+        groups = [torch.distributed.new_group(list(range(g * cpn, (g + 1) * cpn))) for g in range(dp)]
+        if cpn > 1:
+            model.set_cp_info(rank % cpn, cpn, groups[rank // cpn])
     if world > 1:
         model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local_rank], bucket_cap_mb=100,
                                                           gradient_as_bucket_view=True)
     opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
-    g = torch.Generator().manual_seed(1000 + (0 if cp else rank))   # CP: one sequence shared by all ranks
+    # CP: one sequence per context-parallel group, shared by its ranks
+    g = torch.Generator().manual_seed(1000 + (rank // cpn if cp else rank))
     host = [torch.randint(0, 256, (1, seq + 1), generator=g, dtype=torch.long).pin_memory() for _ in range(2)]
     toks = [h.to(dev) for h in host]
     for i in range(args.warmup):
@@ -383,29 +394,37 @@ def run_model(args, rank, world, local_rank, cp=False):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e_steps
     assert lh._native.device_status() == 0
+    clocks = clk.summary()
+    per_rank = None
     if world > 1:
-        t = torch.tensor([ms, e2e_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, e2e_ms = t.tolist()
+        t = torch.tensor([ms, e2e_ms, float(clocks["sm_mhz"] or 0)], device=dev)
+        allr = torch.empty(world, 3, device=dev)
+        torch.distributed.all_gather_into_tensor(allr, t)
+        per_rank = [{"ms_per_step": r[0], "e2e_ms": r[1], "sm_mhz": r[2]} for r in allr.tolist()]
+        ms, e2e_ms = allr[:, :2].max(dim=0).values.tolist()
     if rank != 0:
         return
-    tokens = seq if cp else seq * world
+    tokens = seq * dp if cp else seq * world
     n_layers_lh = sum(1 for i in range(margs.n_layers) if i not in margs.lighthouse_full_attn_layers)
     line = {
-        "metric": "270M train tok/s (Lighthouse norm, k=2048, p=4, L=3)", "value": tokens / (ms * 1e-3),
+        "metric": f"270M train tok/s (Lighthouse norm, k={margs.lighthouse_topk}, p=4, L=3)", "value": tokens / (ms * 1e-3),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "strong" if cp else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": ("strong" if dp == 1 else "weak over dp, strong over cp") if cp else "weak",
+        "vs_baseline": None,
         "dtype": "bf16 autocast, fp32 master",
         "data": "synthetic (uniform random bytes, seeded)",
         "config": {"workload": "llama3_270m_train_step", "params": M.num_params(model), "seq_len": seq,
-                   "global_batch": 1 if cp else world, "lighthouse_layers": n_layers_lh,
-                   "parallelism": f"cp{world} (LighthouseCP + sharded full attention, NCCL)" if cp else f"dp{world} (DDP/NCCL)",
+                   "global_batch": dp if cp else world, "lighthouse_layers": n_layers_lh,
+                   "parallelism": (f"cp{cpn} x dp{dp} (LighthouseCP + sharded full attention, NCCL; DDP across)"
+                                   if cp else f"dp{world} (DDP/NCCL)"),
                    "l2": "activations far larger than L2"},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": (seq + 1) * 8,
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms, "final_loss": loss},
         "gpu_launches": 10 * n_layers_lh * args.steps,
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }
+    if per_rank:
+        line["per_rank"] = per_rank
     print(json.dumps(line), flush=True)
 
 
@@ -676,6 +695,8 @@ def main():
                          "scorer_gla: the `gla` scorer at the layer configuration; "
                          "sweep: config 3's k / L / p sweep, one line per point")
     ap.add_argument("--seq-len", type=int, default=None, help="profiling only: override S")
+    ap.add_argument("--cp", type=int, default=None,
+                    help="model_cp: context-parallel group size (default 2, BASELINE config 5); the rest is data parallel")
     ap.add_argument("--topk", type=int, default=None, help="profiling only: override k")
     args = ap.parse_args()
     if args.seq_len and args.workload in ("layer", "scorer_gla"):

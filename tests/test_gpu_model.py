@@ -75,7 +75,7 @@ def test_model_logits_and_grads_match_oracle_layers(lh, O, cuda, monkeypatch):
     the GPU, math SDPA) on the kernels' own selection.  Only the Lighthouse
     attention differs between the two runs, so the north-star tolerance for
     attention outputs and gradients applies to what reaches the logits and the
-    weights through it."""
+    weights through it.  The oracle run replays the kernel run's selections."""
     from torch.nn.attention import SDPBackend, sdpa_kernel
     from lighthouse_b200 import model as M
     args = M.ModelArgs(dim=256, n_layers=4, n_heads=2, n_kv_heads=2, hidden_dim=384, max_seq_len=4096,
@@ -94,13 +94,24 @@ def test_model_logits_and_grads_match_oracle_layers(lh, O, cuda, monkeypatch):
         loss.backward()
         return logits.detach().float(), {n: p.grad.detach().float() for n, p in m.named_parameters()}
 
+    # run 1: the kernels; record every Lighthouse layer's selection in call
+    # order (a later layer's selection depends on the earlier layers' outputs,
+    # so run 2 must reuse these rather than reselect from its own activations)
+    kernel_layer = M.lighthouse_attention
+    selections = []
+
+    def recording_layer(xq, xk, xv, L, p, k):
+        out, idx = kernel_layer(xq, xk, xv, L, p, k, return_indices=True)
+        selections.append(idx)
+        return out
+
+    monkeypatch.setattr(M, "lighthouse_attention", recording_layer)
     logits, grads = run()
+    assert len(selections) == 3
+    replay = iter(selections)
 
     def oracle_layer(xq, xk, xv, L, p, k):
-        with torch.no_grad():
-            _, _, _, sqk, skq = lh._native.pyramid_score(xq.detach().contiguous(), xk.detach().contiguous(),
-                                                         xv.detach().contiguous(), L, p)
-            idx = lh._native.select_topk(sqk, skq, L, p, k, xq.shape[1])[0]
+        idx = next(replay)
         with torch.autocast("cuda", enabled=False), sdpa_kernel(SDPBackend.MATH):
             out, _ = O.lighthouse_local(xq.float(), xk.float(), xv.float(), L, p, k, indices=idx)
         return out.to(xq.dtype)

@@ -3,24 +3,19 @@
 // Replaces F.scaled_dot_product_attention(q, k, v, is_causal=True) on the
 // gathered sequence (reference src/lighthouse_selection.py:815).
 //
-// One CTA per (pair of 128-row query tiles A and B, b*h), 640 threads,
+// One CTA per (pair of 128-row query tiles A and B, b*h), 384 threads,
 // warp-specialised (warpgroup 0 gives registers to the softmax warpgroups
-// with setmaxnreg: 64 + 4 x 104 per thread-slot = the 5 x 96 of the launch):
+// with setmaxnreg: 56 + 2 x 224 per thread-slot = the 3 x 168 of the launch):
 //   warp 0      TMA producer: Q_A and Q_B once, then K and V tiles through
 //               two-stage rings shared by both query tiles (K one tile ahead)
 //   warp 1      TMEM owner + MMA issuer (one elected lane):
 //                 S_X = Q_X K_j^T  -> TMEM S_X   (SS MMA, both K-major, SW128)
 //                 O_X += P_X V_j   -> TMEM O_X   (TS MMA: P read from TMEM,
 //                                                 V as an MN-major SW128 operand)
-//   warps 4..11 softmax for tile A, warps 12..19 softmax for tile B: two
-//               warpgroups per tile, one per 64-key half of S; a thread owns
-//               one half of a query row (TMEM lane), reads it with tcgen05.ld,
-//               exchanges the half-row maximum with its partner thread through
-//               shared memory, keeps the running max / its partial sum in
-//               registers and writes P (bf16) back over its own S columns with
-//               tcgen05.st.  Two warps per scheduler and tile keep the MUFU
-//               exponentials of one warp overlapped with the other's loads,
-//               maxima and packing.
+//   warps 4..7  softmax for tile A, warps 8..11 softmax for tile B: each thread
+//               owns one query row (= TMEM lane), reads S with tcgen05.ld,
+//               keeps the running max / sum in registers and writes P (bf16)
+//               back over its own S columns with tcgen05.st.
 // The issue order PV_A(j), S_A(j+1), PV_B(j), S_B(j+1) keeps the tensor core
 // busy with one tile while the other tile's softmax runs.  Because S_X(j+1)
 // is issued after PV_X(j), its completion also means O_X is up to date, so a
@@ -45,7 +40,7 @@ constexpr int kD = 128;          // head dim
 constexpr int kBox = 16384;      // one 128 x 64 bf16 TMA box (128-byte rows)
 constexpr int kTileBytes = 2 * kBox;
 constexpr int kNst = 2;          // K/V stages
-constexpr int kThreads = 640;   // 5 warpgroups: {producer, MMA, gate, idle}, softmax A (2), softmax B (2)
+constexpr int kThreads = 384;   // 3 warpgroups: {producer, MMA, 2 idle}, softmax A, softmax B
 __host__ __device__ constexpr uint32_t col_s(int x) { return x ? 128u : 0u; }
 __host__ __device__ constexpr uint32_t col_o(int x) { return x ? 384u : 256u; }
 constexpr uint32_t kTmemCols = 512;
@@ -59,8 +54,6 @@ struct FwdSmem {
   uint64_t s_full[2], p_ready[2], o_final[2];
   uint32_t tmem_base;
   int abort;
-  float rowmax[2][2][fwd::kTile];   // [tile][key half][row]: half-row maxima, exchanged each step
-  float rowsum[2][2][fwd::kTile];   // [tile][key half][row]: partial row sums, exchanged once
 };
 
 __global__ void __launch_bounds__(fwd::kThreads, 1)
@@ -96,7 +89,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     mbar_init(&sm->q_full, 1);
     for (int s = 0; s < kNst; ++s) { mbar_init(&sm->kv_full[s], 1); mbar_init(&sm->k_empty[s], 1); mbar_init(&sm->v_empty[s], 1); }
     mbar_init(&sm->k0_full, 1);
-    for (int x = 0; x < 2; ++x) { mbar_init(&sm->s_full[x], 1); mbar_init(&sm->p_ready[x], 257); mbar_init(&sm->o_final[x], 1); }
+    for (int x = 0; x < 2; ++x) { mbar_init(&sm->s_full[x], 1); mbar_init(&sm->p_ready[x], 129); mbar_init(&sm->o_final[x], 1); }
     sm->abort = 0;
     fence_mbar_init();
   }
@@ -109,7 +102,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   if (warp < 4) {
   // Warpgroup 0 hands registers to the softmax warpgroups (one aligned setmaxnreg per warpgroup).
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 64;\n" ::: "memory");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -158,7 +151,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   } else if (warp == 2) {
     // ------------------------------------------------------------ K/V gate
     // Folds "V_j and K_{j+1} have landed" into p_ready of every tile active at
-    // step j (257 = 256 softmax threads + this warp), so the MMA warp waits
+    // step j (129 = 128 softmax threads + this warp), so the MMA warp waits
     // only on p_ready: each wait of the issuing thread idles the tensor pipe.
     // A phase of p_ready gets this warp's arrival only after the previous one
     // has completed, so an early arrival never counts toward the wrong step.
@@ -193,12 +186,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       const uint32_t v_addr = smem_u32(sV + (j % kNst) * kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < kTile / 16; ++kk)
-        // 16 key rows per step: P columns advance by 8 (two bf16 per column)
-        // inside each 64-key half, whose P sits at the start of that half's own
-        // 64 S columns; V rows advance by 16 x 128 B; the two 64-wide d
-        // blocks sit kBox apart.
-        mma_ts(tbase + col_o(x), tbase + col_s(x) + (kk >> 2) * 64 + (kk & 3) * 8,
-               smem_desc_sw128(v_addr + kk * 2048, kBox, 1024),
+        // 16 key rows per step: P columns advance by 8 (two bf16 per column),
+        // V rows advance by 16 x 128 B; the two 64-wide d blocks sit kBox apart.
+        mma_ts(tbase + col_o(x), tbase + col_s(x) + kk * 8, smem_desc_sw128(v_addr + kk * 2048, kBox, 1024),
                idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
       if (j == nkv_x - 1) mma_commit(&sm->o_final[x]);
     };
@@ -236,10 +226,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
   }
   } else {
-    // ------------------------------------------------------------ softmax (tile A: warps 4-11, B: 12-19)
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 104;\n" ::: "memory");
-    const int x = warp < 12 ? 0 : 1;
-    const int half = ((warp - 4) >> 2) & 1;      // which 64 keys of S (and 64 columns of O) this thread owns
+    // ------------------------------------------------------------ softmax (tile A: warps 4-7, B: 8-11)
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
+    const int x = warp < 8 ? 0 : 1;
     const int my_qt = x ? qt[1] : qt[0];
     const int my_nkv = x ? nkv[1] : nkv[0];
     const int my_qlo = x ? q_lo[1] : q_lo[0];
@@ -248,136 +237,107 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     const int qrow = my_qt * kTile + row;        // row inside this (b,h) slice of Q
     const int qpos = q_off + qrow;               // global causal position
     const uint32_t lane_base = tbase + ((uint32_t)(quad * 32) << 16);
-    const uint32_t s_col = col_s(x) + half * 64, o_col = col_o(x) + half * 64;
-    const uint32_t p_col = s_col;                // P (bf16 pairs) of keys [64 half, +64): first 32 of its S columns
-    const int bar_id = 1 + x;                    // named barrier of this tile's 256 softmax threads
+    const uint32_t s_col = col_s(x), o_col = col_o(x);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    // Every softmax thread of the tile meets the named barrier once per key
-    // tile and once at the end, also after one of its bounded waits failed
-    // (it then skips the work): the two halves of a row must never wait at
-    // the barrier for a partner that has left the loop.
     for (int j = 0; j < my_nkv; ++j) {
-      if (ok) ok = mbar_wait(&sm->s_full[x], j & 1, abort);
-      if (__any_sync(0xffffffffu, !ok)) ok = false;
-      const int kv0 = j * kTile + half * 64;
-      const bool need_mask = (kv0 + 63 > my_qlo) || (kv0 + 64 > S_kv);
-      // Two passes over this thread's 64 S columns, 32 at a time: the row
-      // maximum first, then (after the exchange) the exponentials.  Reading S
-      // from TMEM twice keeps at most 32 of its values in registers.
-      auto load_masked = [&](int c, uint32_t (&sv)[32]) {
-        tmem_ld32(lane_base + s_col + c * 32, sv);
-        tmem_ld_wait();
+      ok = mbar_wait(&sm->s_full[x], j & 1, abort);
+      if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t s[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + s_col + c * 32, s[c]);
+      tmem_ld_wait();
+      const bool need_mask = (j * kTile + kTile - 1 > my_qlo) || (j * kTile + kTile > S_kv);
+      // eight independent partial maxima instead of one 128-long dependency chain
+      float mxp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
         if (need_mask) {
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const int kvpos = kv0 + c * 32 + e;
-            if (kvpos > qpos || kvpos >= S_kv) sv[e] = __float_as_uint(-INFINITY);
+            const int kvpos = j * kTile + c * 32 + e;
+            if (kvpos > qpos || kvpos >= S_kv) s[c][e] = __float_as_uint(-INFINITY);
           }
         }
-      };
-      float mxp[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) mxp[u] = -INFINITY;
-      if (ok) {
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t sv[32];
-          load_masked(c, sv);
-#pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            mxp[(e >> 2) & 3] = fmax3(mxp[(e >> 2) & 3], fmax3(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]),
-                                                                __uint_as_float(sv[e + 2])), __uint_as_float(sv[e + 3]));
-        }
+        for (int e = 0; e < 32; e += 2)
+          mxp[(e >> 1) & 7] = fmax3(mxp[(e >> 1) & 7], __uint_as_float(s[c][e]), __uint_as_float(s[c][e + 1]));
       }
-      const float mx_half = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
-      sm->rowmax[x][half][row] = mx_half;
-      named_bar_sync(bar_id, 256);
-      const float mx = fmaxf(mx_half, sm->rowmax[x][half ^ 1][row]);
-      // the next step's writes to rowmax happen after this tile's next
-      // s_full, which needs this step's p_ready from every thread of the tile
-      if (!ok) continue;
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       const float mx2 = mx * scale2;
-      // O_X already holds PV_X(j-1) (S_X(j) was issued after it) and PV_X(j)
-      // waits for p_ready: O may be rescaled any time before the arrival
-      // below, so it is done after P is stored, when S no longer occupies
-      // registers.  Both halves of a row see the same maxima and decide alike;
-      // each rescales its own 64 columns of O.
-      float alpha = 1.0f;
-      bool rescale = false;
       if (j == 0) {
         m = mx2;
       } else if (__any_sync(0xffffffffu, mx2 > m + 8.0f)) {
+        // O_X already holds PV_X(j-1): S_X(j) was issued after it.
         const float mnew = fmaxf(m, mx2);
-        alpha = ex2(m - mnew);
-        l *= alpha;
-        m = mnew;
-        rescale = true;
-      }
-      // exponent arguments and row sums two lanes at a time (fma.rn.f32x2 / add.rn.f32x2)
-      float2 rsp[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      const float2 sc2 = make_float2(scale2, scale2), negm = make_float2(-m, -m);
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {              // 32 keys at a time: 16 bf16 pairs per tcgen05.st
-        uint32_t sv[32];
-        load_masked(c, sv);
-        uint32_t pk[16];
+        const float alpha = ex2(m - mnew);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float2 a2 = ffma2(make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, negm);
-          const float2 pv = make_float2(ex2(a2.x), ex2(a2.y));
-          rsp[e & 1] = fadd2(rsp[e & 1], pv);
-          pk[e] = pack_bf16(pv.x, pv.y);
-        }
-        tmem_st16(lane_base + p_col + c * 16, pk);
-      }
-      const float2 r = fadd2(rsp[0], rsp[1]);
-      const float rs = r.x + r.y;
-      tmem_st_wait();                            // frees the registers of P before O is touched
-      if (rescale) {
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
           tmem_ld32(lane_base + o_col + c * 32, o);
           tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
           tmem_st32(lane_base + o_col + c * 32, o);
-          tmem_st_wait();
         }
+        l *= alpha;
+        m = mnew;
       }
+      // exponent arguments and row sums two lanes at a time (fma.rn.f32x2 / add.rn.f32x2)
+      float2 rsp[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) rsp[u] = make_float2(0.f, 0.f);
+      const float2 sc2 = make_float2(scale2, scale2), negm = make_float2(-m, -m);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int i0 = h * 64 + 2 * e;
+          const float2 sv = make_float2(__uint_as_float(s[i0 >> 5][i0 & 31]),
+                                        __uint_as_float(s[(i0 + 1) >> 5][(i0 + 1) & 31]));
+          const float2 arg = ffma2(sv, sc2, negm);
+          const float2 pv = make_float2(ex2(arg.x), ex2(arg.y));
+          rsp[e & 3] = fadd2(rsp[e & 3], pv);
+          pk[e] = pack_bf16(pv.x, pv.y);
+        }
+        tmem_st32(lane_base + s_col + h * 32, pk);
+      }
+      const float2 r01 = fadd2(rsp[0], rsp[1]), r23 = fadd2(rsp[2], rsp[3]);
+      const float2 r = fadd2(r01, r23);
+      const float rs = r.x + r.y;
+      tmem_st_wait();
       l += rs;
       tc_fence_before();
       mbar_arrive(&sm->p_ready[x]);
     }
     if (ok && my_nkv > 0) ok = mbar_wait(&sm->o_final[x], 0, abort);
-    // combine the two partial row sums (every thread of the tile takes part)
-    sm->rowsum[x][half][row] = l;
-    named_bar_sync(bar_id, 256);
-    const float l_all = l + sm->rowsum[x][half ^ 1][row];
     if (my_nkv > 0 && !__any_sync(0xffffffffu, !ok)) {
       tc_fence_after();
-      const float inv_l = 1.0f / l_all;
-      __nv_bfloat16* orow = O + ((size_t)bh * S_q + qrow) * kD + half * 64;
-#pragma unroll 1
+      const float inv_l = 1.0f / l;
+      __nv_bfloat16* orow = O + ((size_t)bh * S_q + qrow) * kD;
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t o[16];
-        tmem_ld16(lane_base + o_col + c * 16, o);
+        uint32_t o[32];
+        tmem_ld32(lane_base + o_col + c * 32, o);
         tmem_ld_wait();
         if (qrow < S_q) {
 #pragma unroll
-          for (int v4 = 0; v4 < 2; ++v4) {
+          for (int v4 = 0; v4 < 4; ++v4) {
             uint4 w;
             w.x = pack_bf16(__uint_as_float(o[v4 * 8 + 0]) * inv_l, __uint_as_float(o[v4 * 8 + 1]) * inv_l);
             w.y = pack_bf16(__uint_as_float(o[v4 * 8 + 2]) * inv_l, __uint_as_float(o[v4 * 8 + 3]) * inv_l);
             w.z = pack_bf16(__uint_as_float(o[v4 * 8 + 4]) * inv_l, __uint_as_float(o[v4 * 8 + 5]) * inv_l);
             w.w = pack_bf16(__uint_as_float(o[v4 * 8 + 6]) * inv_l, __uint_as_float(o[v4 * 8 + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(orow + c * 16 + v4 * 8) = w;
+            *reinterpret_cast<uint4*>(orow + c * 32 + v4 * 8) = w;
           }
         }
       }
-      if (qrow < S_q && half == 0) LSE[(size_t)bh * S_q + qrow] = (m + __log2f(l_all)) * 0.69314718055994531f;
+      if (qrow < S_q) LSE[(size_t)bh * S_q + qrow] = (m + __log2f(l)) * 0.69314718055994531f;
     }
   }
 

@@ -1,4 +1,4 @@
-// Hierarchical qk/kq chunked top-k selection, one warp per (b, h, tile).
+// Hierarchical qk/kq chunked top-k selection, one 256-thread CTA per (b, h, tile).
 //
 // Semantics are those of the reference kernel
 // lighthouse_selection_chunked_topk_kernel (src/lighthouse_selection_cuda.py:114-330)
@@ -9,13 +9,15 @@
 // batch order and slot layout (:198-258).  The comparator network is an
 // algorithm that has to be alike; its execution here is different:
 //
-//  * One warp holds the 128 (score, index) pairs in registers, element i at
-//    lane i%32, register i/32.  Stages with j >= 32 are register
-//    compare-exchanges inside a thread, stages with j < 32 are xor shuffles.
-//    No shared memory, no __syncthreads inside the sort.
-//  * The qk sort carries each candidate's kq score as payload, so the kq sort
-//    of the qk rejects needs no dependent global load; the next batch's
-//    scores are prefetched while the current batch sorts.
+//  * Two 128-thread networks run side by side: warps 0-3 hold the qk set
+//    (element i in thread i: score, index and the candidate's kq score as
+//    payload), warps 4-7 the kq set.  The kq sort of batch b's qk rejects and
+//    the qk sort of batch b+1 are independent and run at the same time on
+//    different warps; the rejects cross over through shared memory, so the
+//    kq sort needs no dependent global load.  Stages with j < 32 are xor
+//    shuffles, the three with j >= 32 go through shared memory under a
+//    128-thread named barrier.  The next batch's scores are prefetched while
+//    the current one sorts.
 //  * The reference writes (ordered-float key, value) pairs and sorts them
 //    globally.  In the defined domain every candidate of every level is
 //    written exactly once and the keys order the output as a post-order walk
@@ -23,7 +25,7 @@
 //    whose key c_l*(idx+1) - 2^(1-level) sorts after all its descendants).
 //    So this kernel only records which entries were refined (one bitmap per
 //    level in shared memory), sizes each coarsest entry's subtree, takes a
-//    warp prefix sum and writes the final position-ordered indices directly,
+//    block prefix sum and writes the final position-ordered indices directly,
 //    plus the inverse map used by the scatter and un-pool kernels.  The
 //    per-row torch.sort / torch.gather of the reference disappear.
 #include "lh_common.cuh"
@@ -32,96 +34,66 @@ namespace lh {
 
 constexpr int kSelTopk = 128;
 constexpr int kSelHalf = 64;
+constexpr int kSelThreads = 256;
 constexpr float kNegBig = -1e6f;   // placeholder score (reference :191-194, :227)
 
-// Comparator stages of the descending bitonic network, branch-free.
-// NP = number of payload arrays moved with the key (1: index; 2: index + score).
-// Stages with j < 32 exchange across lanes (xor shuffles); k and j may be
-// run-time values there.
-template <int NP>
-__device__ __forceinline__ void shuffle_stage(int k, int j, int lane, float (&key)[4], float (&pf)[4],
-                                              int (&ix)[4]) {
-  // Integer predicates on purpose: the same logic written with bool ternaries
-  // compiles to a form about four times slower per stage on this target.
-  const int lower = (lane & j) == 0;
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int i = lane + 32 * r;
-    const int desc = (i & k) == 0;
-    const float o = __shfl_xor_sync(0xffffffffu, key[r], j);
-    const int oi = __shfl_xor_sync(0xffffffffu, ix[r], j);
-    float op = 0.f;
-    if (NP > 1) op = __shfl_xor_sync(0xffffffffu, pf[r], j);
-    // lower partner keeps the larger value when descending; strict compares keep ties in place
-    const int lt = key[r] < o, gt = key[r] > o;
-    const int swap = (lower ^ desc) ? gt : lt;
-    key[r] = swap ? o : key[r];
-    ix[r] = swap ? oi : ix[r];
-    if (NP > 1) pf[r] = swap ? op : pf[r];
-  }
+// One element of a 128-wide set: sort key, payload score (qk set: the
+// candidate's kq score) and index.
+struct SelElem { float key; float pf; int ix; };
+
+// Shared-memory exchange buffers of one set: one per stage with j >= 32
+// (k = 64 / j = 32, k = 128 / j = 64, k = 128 / j = 32).  Each buffer is
+// written once per network and read after the group barrier; by the next
+// network's write to it every thread has passed two later barriers.
+struct SelXchg { float key[3][kSelTopk]; float pf[3][kSelTopk]; int ix[3][kSelTopk]; };
+
+// Compare-exchange of element t with element t ^ j (value o) in the stage
+// of bitonic block size k: the lower partner keeps the larger value when
+// descending; strict compares leave ties in place.  Integer predicates, as
+// bool ternaries compile to a slower form on this target.
+template <bool PF>
+__device__ __forceinline__ void cmp_swap(int t, int k, int j, SelElem& e, float ok, float op, int oi) {
+  const int lower = (t & j) == 0, desc = (t & k) == 0;
+  const int lt = e.key < ok, gt = e.key > ok;
+  const int swap = (lower ^ desc) ? gt : lt;
+  e.key = swap ? ok : e.key;
+  e.ix = swap ? oi : e.ix;
+  if (PF) e.pf = swap ? op : e.pf;
 }
 
-// Stages with j >= 32 exchange registers inside a thread; K and J are
-// compile-time so that the register indices are constants.
-template <int NP, int K, int J>
-__device__ __forceinline__ void register_stage(int lane, float (&key)[4], float (&pf)[4], int (&ix)[4]) {
-  constexpr int rr = J >> 5;
-#pragma unroll
-  for (int lo = 0; lo < 4; ++lo) {
-    if (lo & rr) continue;
-    const int hi = lo | rr;
-    const int i_lo = lane + 32 * lo;
-    const int desc = (i_lo & K) == 0;
-    const float a = key[lo], b = key[hi];
-    const int lt = a < b, gt = a > b;
-    const int swap = desc ? lt : gt;
-    key[lo] = swap ? b : a;
-    key[hi] = swap ? a : b;
-    const int ia = ix[lo], ib = ix[hi];
-    ix[lo] = swap ? ib : ia;
-    ix[hi] = swap ? ia : ib;
-    if (NP > 1) {
-      const float pa = pf[lo], pb = pf[hi];
-      pf[lo] = swap ? pb : pa;
-      pf[hi] = swap ? pa : pb;
-    }
-  }
+template <bool PF>
+__device__ __forceinline__ void shfl_stage(int t, int k, int j, SelElem& e) {
+  const float ok = __shfl_xor_sync(0xffffffffu, e.key, j);
+  const int oi = __shfl_xor_sync(0xffffffffu, e.ix, j);
+  const float op = PF ? __shfl_xor_sync(0xffffffffu, e.pf, j) : 0.f;
+  cmp_swap<PF>(t, k, j, e, ok, op, oi);
 }
 
-struct SortSet2 { float key[4]; float pf[4]; int ix[4]; };   // qk sort: key qk, payload kq score + index
-struct SortSet1 { float key[4]; float pf[4]; int ix[4]; };   // kq sort: key kq, payload index
-
-// The network as compact loops: stages with j < 32 take k and j at run time
-// (only the register index is unrolled); the three stages with j >= 32 are
-// spelled out.  A fully unrolled network is tens of KB of straight-line code
-// executed by one warp per SM, which stalls on instruction fetch.
-// NETS = 1: the kq set only; 2: the qk set only; 3: both, stage by stage
-// (two independent networks for instruction-level parallelism).
-template <int NETS>
-__device__ __forceinline__ void shuffle_stage2(int k, int j, int lane, SortSet2& a, SortSet1& b) {
-  if (NETS & 2) shuffle_stage<2>(k, j, lane, a.key, a.pf, a.ix);
-  if (NETS & 1) shuffle_stage<1>(k, j, lane, b.key, b.pf, b.ix);
-}
-template <int NETS, int K, int J>
-__device__ __forceinline__ void register_stage2(int lane, SortSet2& a, SortSet1& b) {
-  if (NETS & 2) register_stage<2, K, J>(lane, a.key, a.pf, a.ix);
-  if (NETS & 1) register_stage<1, K, J>(lane, b.key, b.pf, b.ix);
+template <bool PF>
+__device__ __forceinline__ void smem_stage(int t, int k, int j, int buf, int bar_id, SelElem& e, SelXchg* x) {
+  x->key[buf][t] = e.key;
+  x->ix[buf][t] = e.ix;
+  if (PF) x->pf[buf][t] = e.pf;
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(kSelTopk) : "memory");
+  const int o = t ^ j;
+  cmp_swap<PF>(t, k, j, e, x->key[buf][o], PF ? x->pf[buf][o] : 0.f, x->ix[buf][o]);
 }
 
-template <int NETS>
-__device__ __forceinline__ void bitonic128_sets(int lane, SortSet2& a, SortSet1& b) {
+// The whole 128-wide descending network on the calling 128-thread group.
+template <bool PF>
+__device__ __forceinline__ void bitonic128(int t, int bar_id, SelElem& e, SelXchg* x) {
 #pragma unroll 1
   for (int k = 2; k <= 32; k <<= 1) {
 #pragma unroll 1
-    for (int j = k >> 1; j > 0; j >>= 1) shuffle_stage2<NETS>(k, j, lane, a, b);
+    for (int j = k >> 1; j > 0; j >>= 1) shfl_stage<PF>(t, k, j, e);
   }
-  register_stage2<NETS, 64, 32>(lane, a, b);
+  smem_stage<PF>(t, 64, 32, 0, bar_id, e, x);
 #pragma unroll 1
-  for (int j = 16; j > 0; j >>= 1) shuffle_stage2<NETS>(64, j, lane, a, b);
-  register_stage2<NETS, 128, 64>(lane, a, b);
-  register_stage2<NETS, 128, 32>(lane, a, b);
+  for (int j = 16; j > 0; j >>= 1) shfl_stage<PF>(t, 64, j, e);
+  smem_stage<PF>(t, 128, 64, 1, bar_id, e, x);
+  smem_stage<PF>(t, 128, 32, 2, bar_id, e, x);
 #pragma unroll 1
-  for (int j = 16; j > 0; j >>= 1) shuffle_stage2<NETS>(128, j, lane, a, b);
+  for (int j = 16; j > 0; j >>= 1) shfl_stage<PF>(t, 128, j, e);
 }
 
 struct SelGeom {
@@ -139,23 +111,30 @@ __device__ __forceinline__ bool refined(const uint32_t* bm, const int* bm_off, c
   return (bm[bm_off[lev] + (rel >> 5)] >> (rel & 31)) & 1u;
 }
 
-__global__ void __launch_bounds__(32)
+__global__ void __launch_bounds__(kSelThreads)
 select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ sk_all, SelGeom g,
                    Pyramid pyr, int32_t* __restrict__ indices, int32_t* __restrict__ inverse) {
-  extern __shared__ uint32_t s_dyn[];
-  int* s_parent = reinterpret_cast<int*>(s_dyn);            // [128]
-  int* s_bmoff = reinterpret_cast<int*>(s_dyn + kSelTopk);  // [8] bitmap word offset per level
-  int* s_lvloff = s_bmoff + 8;                              // [8] pyramid offset per level
-  uint32_t* s_bm = s_dyn + kSelTopk + 16;                   // refinement bitmaps
-  const int lane = threadIdx.x;
+  extern __shared__ __align__(16) uint32_t s_dyn[];
+  SelXchg* s_x = reinterpret_cast<SelXchg*>(s_dyn);                   // [2]: qk group, kq group
+  float* s_rej_pf = reinterpret_cast<float*>(s_x + 2);                 // [2][64] qk rejects: kq score
+  int* s_rej_ix = reinterpret_cast<int*>(s_rej_pf + 2 * kSelHalf);     // [2][64] qk rejects: index
+  int* s_parent = s_rej_ix + 2 * kSelHalf;                             // [128]
+  int* s_bmoff = s_parent + kSelTopk;                                  // [8] bitmap word offset per level
+  int* s_lvloff = s_bmoff + 8;                                         // [8] pyramid offset per level
+  int* s_scan = s_lvloff + 8;                                          // [8] per-warp totals
+  uint32_t* s_bm = reinterpret_cast<uint32_t*>(s_scan + 8);            // refinement bitmaps
+  const int tid = threadIdx.x;
+  const int grp = tid >> 7;                       // 0: qk set, 1: kq set
+  const int t = tid & 127;                        // element of the set
+  const int bar_id = 1 + grp;
   const int bh = blockIdx.x / g.T;
   const int tile = blockIdx.x % g.T;
   const float* sq = sq_all + (size_t)bh * g.S_tot;
   const float* sk = sk_all + (size_t)bh * g.S_tot;
-  for (int w = lane; w < g.bm_words; w += 32) s_bm[w] = 0u;
-  for (int i = lane; i < kSelTopk; i += 32) s_parent[i] = -1;
-  if (lane < 8) { s_bmoff[lane] = g.bm_word_off[lane]; s_lvloff[lane] = pyr.off[lane]; }
-  __syncwarp();
+  for (int w = tid; w < g.bm_words; w += kSelThreads) s_bm[w] = 0u;
+  if (tid < kSelTopk) s_parent[tid] = -1;
+  if (tid < 8) { s_bmoff[tid] = g.bm_word_off[tid]; s_lvloff[tid] = pyr.off[tid]; }
+  __syncthreads();
 
   const int pmask = g.p - 1;
   for (int lev = g.L; lev >= 2; --lev) {
@@ -163,83 +142,81 @@ select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ s
     const int K_end = (g.N >> ((lev - 1) * g.shift)) - 1;    // last entry of this level
     const int ncand = (lev == g.L) ? g.ncc : g.p * kSelTopk;
     const int tile_start = tile * g.ncc;
-    auto cand = [&](int c) -> int {
-      if (c >= ncand) return -1;
-      if (lev == g.L) return tile_start + c;
-      const int pv = s_parent[c >> g.shift];
-      if (pv < 0) return -1;
-      const int kidx = pv * g.p + (c & pmask);
-      return (kidx > K_end) ? -1 : kidx;
-    };
-    auto valid = [&](int kidx) { return kidx >= 0 && kidx <= K_end; };
-
-    // qk set: regs 0,1 = running top-64 by qk, regs 2,3 = the batch being sorted.
-    // kq set: regs 0,1 = running top-64 by kq, regs 2,3 = the qk rejects.
-    SortSet2 qk;
-    SortSet1 kq;
-#pragma unroll
-    for (int r = 0; r < 4; ++r) { qk.key[r] = kNegBig; qk.pf[r] = kNegBig; qk.ix[r] = -1; kq.key[r] = kNegBig; kq.pf[r] = 0.f; kq.ix[r] = -1; }
-
+    // qk elements 0..63: running top-64 by qk, 64..127: the batch being sorted.
+    // kq elements 0..63: running top-64 by kq, 64..127: the qk rejects.
+    SelElem e;
+    e.key = kNegBig;
+    e.pf = grp == 0 ? kNegBig : 0.f;
+    e.ix = -1;
     const int nb = (ncand + kSelHalf - 1) / kSelHalf;
-    int nidx[2];
-    float nq[2], nk[2];
+    // qk threads 64..127 fetch candidate bt * 64 + (t - 64) of each batch
+    int nidx = -1;
+    float nq = kNegBig, nk = kNegBig;
     auto fetch = [&](int bt) {
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        nidx[r] = cand(bt * kSelHalf + lane + 32 * r);
-        nq[r] = valid(nidx[r]) ? __ldg(sq + lvl_off + nidx[r]) : kNegBig;
-        nk[r] = valid(nidx[r]) ? __ldg(sk + lvl_off + nidx[r]) : kNegBig;
+      const int c = bt * kSelHalf + t - kSelHalf;
+      int kidx = -1;
+      if (c < ncand) {
+        if (lev == g.L) {
+          kidx = tile_start + c;
+        } else {
+          const int pv = s_parent[c >> g.shift];
+          if (pv >= 0) kidx = pv * g.p + (c & pmask);
+        }
+      }
+      nidx = -1; nq = kNegBig; nk = kNegBig;
+      if (kidx >= 0 && kidx <= K_end) {
+        nidx = kidx;
+        nq = __ldg(sq + lvl_off + kidx);
+        nk = __ldg(sk + lvl_off + kidx);
       }
     };
-    auto take = [&]() {
-#pragma unroll
-      for (int r = 0; r < 2; ++r) { qk.ix[2 + r] = nidx[r]; qk.key[2 + r] = nq[r]; qk.pf[2 + r] = nk[r]; }
-    };
-    fetch(0);
-    take();
-    if (nb > 1) fetch(1);
-    // qk sort of batch 0 (reference :203-232)
-    bitonic128_sets<2>(lane, qk, kq);
+    const bool loader = grp == 0 && t >= kSelHalf;
+    if (loader) {
+      fetch(0);
+      e.ix = nidx; e.key = nq; e.pf = nk;        // batch 0 joins the qk set
+      if (nb > 1) fetch(1);
+    }
+    if (grp == 0) bitonic128<true>(t, bar_id, e, &s_x[0]);     // qk sort of batch 0 (reference :203-232)
     for (int bt = 0; bt < nb; ++bt) {
-      // kq set for batch bt: its top-64 and the qk rejects (reference :242-250)
-#pragma unroll
-      for (int r = 0; r < 2; ++r) { kq.key[2 + r] = qk.pf[2 + r]; kq.ix[2 + r] = qk.ix[2 + r]; }
-      if (bt + 1 < nb) {
-        take();                                  // batch bt+1 joins the qk top-64
-        if (bt + 2 < nb) fetch(bt + 2);
-        // kq sort of batch bt and qk sort of batch bt+1 are independent: run them together
-        bitonic128_sets<3>(lane, qk, kq);
+      // the qk rejects of batch bt (elements 64..127) cross to the kq set (reference :242-250)
+      if (loader) { s_rej_pf[(bt & 1) * kSelHalf + t - kSelHalf] = e.pf; s_rej_ix[(bt & 1) * kSelHalf + t - kSelHalf] = e.ix; }
+      __syncthreads();
+      if (grp == 1 && t >= kSelHalf) {
+        e.key = s_rej_pf[(bt & 1) * kSelHalf + t - kSelHalf];
+        e.ix = s_rej_ix[(bt & 1) * kSelHalf + t - kSelHalf];
+      }
+      if (grp == 0) {
+        if (bt + 1 < nb) {
+          if (loader) {
+            e.ix = nidx; e.key = nq; e.pf = nk;  // batch bt+1 joins the qk top-64
+            if (bt + 2 < nb) fetch(bt + 2);
+          }
+          bitonic128<true>(t, bar_id, e, &s_x[0]);
+        }
       } else {
-        bitonic128_sets<1>(lane, qk, kq);
+        bitonic128<false>(t, bar_id, e, &s_x[1]);
       }
     }
-    int tki[2], ix[2];
-    tki[0] = kq.ix[0]; tki[1] = kq.ix[1];
-    ix[0] = qk.ix[0]; ix[1] = qk.ix[1];
-    __syncwarp();
+    __syncthreads();                              // every read of s_parent for this level is done
     // Parents of the next level: [top-64 by qk ; top-64 by kq] (reference :324-327)
-    s_parent[lane] = ix[0];
-    s_parent[32 + lane] = ix[1];
-    s_parent[64 + lane] = tki[0];
-    s_parent[96 + lane] = tki[1];
-    const int start = tile * (g.ncc << ((g.L - lev) * g.shift));
-    const int kept[4] = {ix[0], ix[1], tki[0], tki[1]};
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int rel = kept[r] - start;
-      if (kept[r] >= 0) atomicOr(&s_bm[s_bmoff[lev] + (rel >> 5)], 1u << (rel & 31));
+    if (t < kSelHalf) {
+      s_parent[grp * kSelHalf + t] = e.ix;
+      const int start = tile * (g.ncc << ((g.L - lev) * g.shift));
+      const int rel = e.ix - start;
+      if (e.ix >= 0) atomicOr(&s_bm[s_bmoff[lev] + (rel >> 5)], 1u << (rel & 31));
     }
-    __syncwarp();
+    __syncthreads();
   }
 
   // ---- placement: post-order walk of each coarsest entry's refinement tree.
   // Stackless: children of (lev, idx) are (lev-1, idx*p .. idx*p+p-1), so the
   // walk descends to the first child of refined nodes, steps to the next
   // sibling, and climbs to (and emits) the parent after its last child.
-  const int per_lane = g.ncc / 32;
-  const int e0 = tile * g.ncc + lane * per_lane;
-  auto walk = [&](int e, auto&& visit) {
-    int lev = g.L, idx = e;
+  const int per = (g.ncc + kSelThreads - 1) / kSelThreads;
+  const int e0 = tile * g.ncc + min(tid * per, g.ncc);
+  const int e1 = tile * g.ncc + min(tid * per + per, g.ncc);
+  auto walk = [&](int en, auto&& visit) {
+    int lev = g.L, idx = en;
     while (lev >= 2 && refined(s_bm, s_bmoff, g, lev, idx, tile)) { idx <<= g.shift; --lev; }
     while (true) {
       visit(lev, idx);
@@ -254,18 +231,24 @@ select_topk_kernel(const float* __restrict__ sq_all, const float* __restrict__ s
     }
   };
   int count = 0;
-  for (int e = e0; e < e0 + per_lane; ++e) walk(e, [&](int, int) { ++count; });
+  for (int en = e0; en < e1; ++en) walk(en, [&](int, int) { ++count; });
+  // block exclusive prefix sum of the counts (thread order = entry order)
+  const int lane = tid & 31, warp = tid >> 5;
   int incl = count;
 #pragma unroll
   for (int m = 1; m < 32; m <<= 1) {
     const int v = __shfl_up_sync(0xffffffffu, incl, m);
     if (lane >= m) incl += v;
   }
-  int slot = tile * g.chunk_len + incl - count;
+  if (lane == 31) s_scan[warp] = incl;
+  __syncthreads();
+  int before = 0;
+  for (int w = 0; w < warp; ++w) before += s_scan[w];
+  int slot = tile * g.chunk_len + before + incl - count;
   int32_t* out = indices + (size_t)bh * g.S_sel;
   int32_t* inv = inverse ? inverse + (size_t)bh * g.S_tot : nullptr;
-  for (int e = e0; e < e0 + per_lane; ++e) {
-    walk(e, [&](int lev, int idx) {
+  for (int en = e0; en < e1; ++en) {
+    walk(en, [&](int lev, int idx) {
       const int pidx = idx + s_lvloff[lev - 1];
       out[slot] = pidx;
       if (inv) inv[pidx] = slot;
@@ -310,14 +293,14 @@ int select_topk(const float* sqk, const float* skq, int B, int H, int S, int L, 
   SelGeom g; Pyramid pyr;
   int rc = select_geometry(S, L, p, k, &g, &pyr);
   if (rc) return rc;
-  const size_t smem = (kSelTopk + 16 + (size_t)g.bm_words) * sizeof(uint32_t);
+  const size_t smem = 2 * sizeof(SelXchg) + (4 * kSelHalf + kSelTopk + 24 + (size_t)g.bm_words) * sizeof(uint32_t);
   if (smem > 200 * 1024) { set_error("select: refinement bitmaps exceed shared memory"); return LH_ERR_SHAPE; }
   if (smem > 48 * 1024) cudaFuncSetAttribute(select_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (inverse) {
     cudaError_t e = cudaMemsetAsync(inverse, 0xff, sizeof(int32_t) * (size_t)B * H * g.S_tot, st);
     if (e != cudaSuccess) { set_error("select: memset inverse: %s", cudaGetErrorString(e)); return LH_ERR_LAUNCH; }
   }
-  select_topk_kernel<<<B * H * g.T, 32, smem, st>>>(sqk, skq, g, pyr, indices, inverse);
+  select_topk_kernel<<<B * H * g.T, kSelThreads, smem, st>>>(sqk, skq, g, pyr, indices, inverse);
   return check_launch("select_topk_kernel");
 }
 

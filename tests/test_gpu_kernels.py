@@ -181,3 +181,31 @@ def test_grouped_scatter_and_unpool_vs_oracle(lh, O, cuda, shape):
     _, _, qc, _, _ = O.norm_scorer(x, x, x, p, L)
     O.gather_rows(qc, idx).backward(dsel.float())
     assert _rel_close(dxq.float(), x.grad, BF16_ULP, 1e-6).all()
+
+
+def test_select_faster_than_reference_kernel(lh, O, cuda):
+    """BASELINE config 3 shape (S=131072, L=3, p=4, k=2048, H=8): the product
+    selection (indices + inverse map, one launch) against the reference
+    kernel compiled from its own source plus its stable sort and gather
+    (CU:404-427), CUDA events on the current stream, 20 launches each after
+    3 warm-up launches.  Prints both times; asserts the product is faster."""
+    N, L, p, k = 131072, 3, 4, 2048
+    sq, sk = make_scores(1, 8, N, L, p, "bf16norm", 5)
+    sq, sk = sq.to(cuda), sk.to(cuda)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(20):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / 20
+
+    ours = timed(lambda: lh._native.select_topk(sq, sk, L, p, k, N))
+    ref = timed(lambda: O.ref_select_gpu(sq, sk, L, p, k, N))
+    print(f"\nselection at S=131072, k=2048, H=8: product {ours * 1e3:.1f} us, reference kernel + sort/gather "
+          f"{ref * 1e3:.1f} us")
+    assert ours < ref

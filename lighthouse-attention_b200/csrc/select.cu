@@ -79,20 +79,21 @@ __device__ __forceinline__ void smem_stage(int t, int k, int j, int buf, int bar
   cmp_swap<PF>(t, k, j, e, x->key[buf][o], PF ? x->pf[buf][o] : 0.f, x->ix[buf][o]);
 }
 
-// The whole 128-wide descending network on the calling 128-thread group.
+// The whole 128-wide descending network on the calling 128-thread group,
+// fully unrolled (one element per thread keeps it a few hundred instructions).
 template <bool PF>
 __device__ __forceinline__ void bitonic128(int t, int bar_id, SelElem& e, SelXchg* x) {
-#pragma unroll 1
+#pragma unroll
   for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll 1
+#pragma unroll
     for (int j = k >> 1; j > 0; j >>= 1) shfl_stage<PF>(t, k, j, e);
   }
   smem_stage<PF>(t, 64, 32, 0, bar_id, e, x);
-#pragma unroll 1
+#pragma unroll
   for (int j = 16; j > 0; j >>= 1) shfl_stage<PF>(t, 64, j, e);
   smem_stage<PF>(t, 128, 64, 1, bar_id, e, x);
   smem_stage<PF>(t, 128, 32, 2, bar_id, e, x);
-#pragma unroll 1
+#pragma unroll
   for (int j = 16; j > 0; j >>= 1) shfl_stage<PF>(t, 128, j, e);
 }
 

@@ -169,6 +169,20 @@ int lh_scatter_bwd(const void* dout, const int32_t* indices, int dtype,
                    int B, int H, int S_sel, int D, int N_shard, int N_total, int L, int p,
                    void* dattn, void* stream);
 
+/* lh_scatter_fwd / lh_scatter_bwd with the base-position tensor in token-major
+ * layout (B, N_total, H, D) instead of (B, H, N_total, D).  The reference's
+ * call site transposes the layer output to (B, S, H*D) before the output
+ * projection (lighthouse-attention.patch:737); written token-major, that
+ * transpose is a view.  Needs D * element size of 256 or 512 bytes and
+ * B*H divisible by the heads one warp covers (2 for bf16 D=128), else
+ * LH_ERR_SHAPE. */
+int lh_scatter_fwd_token_major(const void* attn, const int32_t* inverse, int dtype,
+                               int B, int H, int S_sel, int D, int N_shard, int N_total,
+                               int num_levels, int pooling_factor, void* out, void* stream);
+int lh_scatter_bwd_token_major(const void* dout, const int32_t* indices, int dtype,
+                               int B, int H, int S_sel, int D, int N_shard, int N_total,
+                               int num_levels, int pooling_factor, void* dattn, void* stream);
+
 /* Backward of gather + pyramid means: for each raw token t and head h,
  *   dx[b,t,h] = dsel[inv(t)] + sum_{l>=1} dsel[inv(off_l + t/p^l)] / p^l
  * (absent entries contribute 0).  Replaces the autograd of the three gathers

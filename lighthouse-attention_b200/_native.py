@@ -44,6 +44,8 @@ _SIGS = {
     "lh_attn_bwd_noalloc": (ctypes.c_int, [_VP] * 6 + [ctypes.c_int] * 6 + [ctypes.c_float] + [_VP] * 4),
     "lh_scatter_fwd": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
     "lh_scatter_bwd": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
+    "lh_scatter_fwd_token_major": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
+    "lh_scatter_bwd_token_major": (ctypes.c_int, [_VP, _VP] + [ctypes.c_int] * 9 + [_VP, _VP]),
     "lh_unpool_bwd": (ctypes.c_int, [_VP] * 4 + [ctypes.c_int] * 8 + [_VP] * 4),
     "lh_rope_apply": (ctypes.c_int, [_VP] * 5 + [ctypes.c_int] * 6 + [_VP]),
     "lh_simple_gla_fwd": (ctypes.c_int, [_VP] * 8 + [ctypes.c_int] * 5 + [ctypes.c_float, _VP]),
@@ -225,6 +227,33 @@ def scatter_fwd(attn, inverse, N_shard: int, N_total: int, L: int, p: int):
     _check(load().lh_scatter_fwd(_ptr(attn), _ptr(inverse), LH_DTYPE[attn.dtype], B, H, S_sel, D, N_shard, N_total,
                                  L, p, _ptr(out), _stream()))
     return out
+
+
+def token_major_ok(B: int, H: int, D: int, dtype) -> bool:
+    """Whether the token-major scatter kernels cover this geometry."""
+    row = D * (2 if dtype == torch.bfloat16 else 4)
+    return row in (256, 512) and (B * H) % (32 // (row // 16)) == 0
+
+
+def scatter_fwd_token_major(attn, inverse, N_shard: int, N_total: int, L: int, p: int):
+    """scatter_fwd with the output as (B, N_total, H, D) (token-major)."""
+    attn = attn.contiguous()
+    B, H, S_sel, D = attn.shape
+    out = torch.empty(B, N_total, H, D, dtype=attn.dtype, device=attn.device)
+    _check(load().lh_scatter_fwd_token_major(_ptr(attn), _ptr(inverse), LH_DTYPE[attn.dtype], B, H, S_sel, D,
+                                             N_shard, N_total, L, p, _ptr(out), _stream()))
+    return out
+
+
+def scatter_bwd_token_major(dout, indices, N_shard: int, N_total: int, L: int, p: int):
+    """scatter_bwd for dout given as (B, N_total, H, D) (token-major)."""
+    dout = dout.contiguous()
+    B, _, H, D = dout.shape
+    S_sel = indices.shape[-1]
+    dattn = torch.empty(B, H, S_sel, D, dtype=dout.dtype, device=dout.device)
+    _check(load().lh_scatter_bwd_token_major(_ptr(dout), _ptr(indices), LH_DTYPE[dout.dtype], B, H, S_sel, D,
+                                             N_shard, N_total, L, p, _ptr(dattn), _stream()))
+    return dattn
 
 
 def scatter_bwd(dout, indices, N_shard: int, N_total: int, L: int, p: int):

@@ -54,6 +54,8 @@ int gather_selected(const void*, const void*, const void*, const void*, const vo
                     int, int, int, int, const int32_t*, int, void*, void*, void*, cudaStream_t);
 int scatter_fwd(const void*, const int32_t*, int, int, int, int, int, int, int, int, int, void*, cudaStream_t);
 int scatter_bwd(const void*, const int32_t*, int, int, int, int, int, int, int, int, int, void*, cudaStream_t);
+int scatter_fwd_layout(const void*, const int32_t*, int, int, int, int, int, int, int, int, int, int, void*, cudaStream_t);
+int scatter_bwd_layout(const void*, const int32_t*, int, int, int, int, int, int, int, int, int, int, void*, cudaStream_t);
 int build_inverse(const int32_t*, int, int, int, int, int32_t*, cudaStream_t);
 int unpool_bwd(const void*, const void*, const void*, const int32_t*, int, int, int, int, int, int, int, int,
                void*, void*, void*, cudaStream_t);
@@ -208,6 +210,24 @@ int lh_scatter_bwd(const void* dout, const int32_t* indices, int dtype, int B, i
   LH_REQUIRE(p >= 2 && (p & (p - 1)) == 0 && L >= 1 && L <= 7, LH_ERR_SHAPE, "scatter_bwd: bad L/p");
   LH_ARCH();
   return scatter_bwd(dout, indices, dtype, B, H, S_sel, D, N_shard, N_total, L, p, dattn, S_(stream));
+}
+
+int lh_scatter_fwd_token_major(const void* attn, const int32_t* inverse, int dtype, int B, int H, int S_sel, int D,
+                               int N_shard, int N_total, int L, int p, void* out, void* stream) {
+  g_err[0] = 0;
+  LH_REQUIRE(attn && inverse && out, LH_ERR_ARG, "scatter_fwd: null pointer");
+  LH_REQUIRE(p >= 2 && (p & (p - 1)) == 0 && L >= 1 && L <= 7, LH_ERR_SHAPE, "scatter_fwd: bad L/p");
+  LH_ARCH();
+  return scatter_fwd_layout(attn, inverse, dtype, B, H, S_sel, D, N_shard, N_total, L, p, 1, out, S_(stream));
+}
+
+int lh_scatter_bwd_token_major(const void* dout, const int32_t* indices, int dtype, int B, int H, int S_sel, int D,
+                               int N_shard, int N_total, int L, int p, void* dattn, void* stream) {
+  g_err[0] = 0;
+  LH_REQUIRE(dout && indices && dattn, LH_ERR_ARG, "scatter_bwd: null pointer");
+  LH_REQUIRE(p >= 2 && (p & (p - 1)) == 0 && L >= 1 && L <= 7, LH_ERR_SHAPE, "scatter_bwd: bad L/p");
+  LH_ARCH();
+  return scatter_bwd_layout(dout, indices, dtype, B, H, S_sel, D, N_shard, N_total, L, p, 1, dattn, S_(stream));
 }
 
 int lh_unpool_bwd(const void* dq, const void* dk, const void* dv, const int32_t* inverse, int dtype, int B,

@@ -187,7 +187,8 @@ grouped_rows_kernel(const T* __restrict__ s0, const T* __restrict__ s1, const T*
 template <class T>
 __global__ void __launch_bounds__(kRowThreads)
 scatter_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ indices, Pyramid pyr, int p_shift,
-                   int D, FastDiv fd_ssel, int N_total, T* __restrict__ dattn, int cpr_shift, uint32_t n_chunks) {
+                   int D, FastDiv fd_ssel, int N_total, T* __restrict__ dattn, int cpr_shift, uint32_t n_chunks,
+                   int H, long long row_stride, long long b_stride, long long h_stride) {
   constexpr int VEC = Vec16<T>::N;
   for (uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x; gid < n_chunks; gid += gridDim.x * blockDim.x) {
     const uint32_t row = gid >> cpr_shift;          // bh * S_sel + s
@@ -206,13 +207,14 @@ scatter_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ indic
         const int f = 1 << (l * p_shift);
         const int first = (idx - lvl_off) * f + f - 1;
         const int last = min(first + f, N_total);
-        const T* src = dout + (size_t)bh * N_total * D + c;
+        const int b = (int)bh / H, h = (int)bh - b * H;
+        const T* src = dout + b * b_stride + h * h_stride + c;
         // four independent loads in flight per trip; the fp32 sum keeps position order
         int pos = first;
         for (; pos + 4 <= last; pos += 4) {
           float v[4][VEC];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) load16(src + (size_t)(pos + u) * D, v[u]);
+          for (int u = 0; u < 4; ++u) load16(src + (size_t)(pos + u) * row_stride, v[u]);
 #pragma unroll
           for (int u = 0; u < 4; ++u)
 #pragma unroll
@@ -220,7 +222,7 @@ scatter_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ indic
         }
         for (; pos < last; ++pos) {
           float v[VEC];
-          load16(src + (size_t)pos * D, v);
+          load16(src + (size_t)pos * row_stride, v);
 #pragma unroll
           for (int e = 0; e < VEC; ++e) acc[e] += v[e];
         }
@@ -383,17 +385,26 @@ int gather_selected(const void* qr, const void* kr, const void* vr, const void* 
   return check_launch("gather_kernel");
 }
 
-int scatter_fwd(const void* attn, const int32_t* inverse, int dtype, int B, int H, int S_sel, int D,
-                int N_shard, int N_total, int L, int p, void* out, cudaStream_t st) {
+// token_major = 0: out is (B, H, N_total, D); 1: out is (B, N_total, H, D), the
+// layout the output projection reads (the transpose after the layer,
+// lighthouse-attention.patch:737, becomes a view).
+int scatter_fwd_layout(const void* attn, const int32_t* inverse, int dtype, int B, int H, int S_sel, int D,
+                       int N_shard, int N_total, int L, int p, int token_major, void* out, cudaStream_t st) {
   Pyramid pyr; pyr.init(N_shard, L, p);
   if (!aligned16(attn) || !aligned16(out)) { set_error("scatter_fwd: pointers must be 16-byte aligned"); return LH_ERR_ARG; }
   int cs; uint32_t n;
   int rc = row_geometry("scatter_fwd", dtype, D, (long long)B * H * N_total, &cs, &n);
   if (rc) return rc;
+  const long long row_stride = token_major ? (long long)H * D : D;
+  const long long b_stride = (long long)H * N_total * D;
+  const long long h_stride = token_major ? D : (long long)N_total * D;
   if (launch_grouped_rows<true>(dtype, L, cs, attn, nullptr, nullptr, out, nullptr, nullptr, 1, inverse, pyr,
-                                log2i(p), D, S_sel, N_total, B, H, D, (long long)H * N_total * D,
-                                (long long)N_total * D, st))
+                                log2i(p), D, S_sel, N_total, B, H, row_stride, b_stride, h_stride, st))
     return check_launch("scatter_fwd (grouped)");
+  if (token_major) {
+    set_error("scatter_fwd: the token-major layout needs 256- or 512-byte rows and B*H divisible by the heads per warp");
+    return LH_ERR_SHAPE;
+  }
   FastDiv fn(N_total);
   auto go = [&](auto lv) {
     constexpr int LV = decltype(lv)::value;
@@ -406,19 +417,33 @@ int scatter_fwd(const void* attn, const int32_t* inverse, int dtype, int B, int 
   return check_launch("scatter_fwd");
 }
 
-int scatter_bwd(const void* dout, const int32_t* indices, int dtype, int B, int H, int S_sel, int D,
-                int N_shard, int N_total, int L, int p, void* dattn, cudaStream_t st) {
+int scatter_fwd(const void* attn, const int32_t* inverse, int dtype, int B, int H, int S_sel, int D,
+                int N_shard, int N_total, int L, int p, void* out, cudaStream_t st) {
+  return scatter_fwd_layout(attn, inverse, dtype, B, H, S_sel, D, N_shard, N_total, L, p, 0, out, st);
+}
+
+// token_major as for scatter_fwd_layout, for dout.
+int scatter_bwd_layout(const void* dout, const int32_t* indices, int dtype, int B, int H, int S_sel, int D,
+                       int N_shard, int N_total, int L, int p, int token_major, void* dattn, cudaStream_t st) {
   Pyramid pyr; pyr.init(N_shard, L, p);
   if (!aligned16(dout) || !aligned16(dattn)) { set_error("scatter_bwd: pointers must be 16-byte aligned"); return LH_ERR_ARG; }
   int cs; uint32_t n;
   int rc = row_geometry("scatter_bwd", dtype, D, (long long)B * H * S_sel, &cs, &n);
   if (rc) return rc;
   FastDiv fs(S_sel);
+  const long long row_stride = token_major ? (long long)H * D : D;
+  const long long b_stride = (long long)H * N_total * D;
+  const long long h_stride = token_major ? D : (long long)N_total * D;
   if (dtype == LH_DTYPE_BF16)
-    scatter_bwd_kernel<__nv_bfloat16><<<grid_for(n), kRowThreads, 0, st>>>((const __nv_bfloat16*)dout, indices, pyr, log2i(p), D, fs, N_total, (__nv_bfloat16*)dattn, cs, n);
+    scatter_bwd_kernel<__nv_bfloat16><<<grid_for(n), kRowThreads, 0, st>>>((const __nv_bfloat16*)dout, indices, pyr, log2i(p), D, fs, N_total, (__nv_bfloat16*)dattn, cs, n, H, row_stride, b_stride, h_stride);
   else
-    scatter_bwd_kernel<float><<<grid_for(n), kRowThreads, 0, st>>>((const float*)dout, indices, pyr, log2i(p), D, fs, N_total, (float*)dattn, cs, n);
+    scatter_bwd_kernel<float><<<grid_for(n), kRowThreads, 0, st>>>((const float*)dout, indices, pyr, log2i(p), D, fs, N_total, (float*)dattn, cs, n, H, row_stride, b_stride, h_stride);
   return check_launch("scatter_bwd_kernel");
+}
+
+int scatter_bwd(const void* dout, const int32_t* indices, int dtype, int B, int H, int S_sel, int D,
+                int N_shard, int N_total, int L, int p, void* dattn, cudaStream_t st) {
+  return scatter_bwd_layout(dout, indices, dtype, B, H, S_sel, D, N_shard, N_total, L, p, 0, dattn, st);
 }
 
 int build_inverse(const int32_t* indices, int B, int H, int S_sel, int S_tot, int32_t* inverse, cudaStream_t st) {

@@ -134,6 +134,30 @@ def _(dout, indices, N_shard, N_total, L, p):
     return dout.new_empty(B, H, indices.shape[-1], D)
 
 
+@torch.library.custom_op(f"{NS}::scatter_fwd_token_major", mutates_args=())
+def scatter_fwd_token_major(attn: Tensor, inverse: Tensor, N_shard: int, N_total: int, L: int, p: int) -> Tensor:
+    """scatter_fwd with the output as (B, N_total, H, D)."""
+    return _native.scatter_fwd_token_major(attn, inverse, N_shard, N_total, L, p)
+
+
+@scatter_fwd_token_major.register_fake
+def _(attn, inverse, N_shard, N_total, L, p):
+    B, H, _, D = attn.shape
+    return attn.new_empty(B, N_total, H, D)
+
+
+@torch.library.custom_op(f"{NS}::scatter_bwd_token_major", mutates_args=())
+def scatter_bwd_token_major(dout: Tensor, indices: Tensor, N_shard: int, N_total: int, L: int, p: int) -> Tensor:
+    """Adjoint of scatter_fwd_token_major: dout (B, N_total, H, D)."""
+    return _native.scatter_bwd_token_major(dout, indices, N_shard, N_total, L, p)
+
+
+@scatter_bwd_token_major.register_fake
+def _(dout, indices, N_shard, N_total, L, p):
+    B, _, H, D = dout.shape
+    return dout.new_empty(B, H, indices.shape[-1], D)
+
+
 @torch.library.custom_op(f"{NS}::unpool_bwd", mutates_args=())
 def unpool_bwd(dq: Tensor, dk: Tensor, dv: Tensor, inverse: Tensor, S: int, L: int,
                p: int) -> tuple[Tensor, Tensor, Tensor]:

@@ -231,7 +231,13 @@ class _LighthouseLayerFn(torch.autograd.Function):
         qs, ks, vs = _ops.gather_selected(xq, xk, xv, pq, pk, pv, idx)
         scale = 1.0 / math.sqrt(D)
         o, lse = _ops.attn_fwd(qs, ks, vs, scale)
-        out = _ops.scatter_fwd(o, inv, S, S, L, p)
+        # Token-major output (B, S, H, D), returned as a (B, H, S, D) view: the
+        # caller's transpose before the output projection (PATCH:737) is then
+        # free.  Same values as the (B, H, S, D) kernel.
+        if _native.token_major_ok(B, H, D, o.dtype):
+            out = _ops.scatter_fwd_token_major(o, inv, S, S, L, p).transpose(1, 2)
+        else:
+            out = _ops.scatter_fwd(o, inv, S, S, L, p)
         ctx.save_for_backward(qs, ks, vs, o, lse, idx, inv)
         ctx.args = (S, L, p, scale)
         ctx.mark_non_differentiable(idx)
@@ -241,7 +247,11 @@ class _LighthouseLayerFn(torch.autograd.Function):
     def backward(ctx, dout, _didx):
         qs, ks, vs, o, lse, idx, inv = ctx.saved_tensors
         S, L, p, scale = ctx.args
-        dattn = _ops.scatter_bwd(dout.contiguous(), idx, S, S, L, p)
+        B, H, _, D = dout.shape
+        if not dout.is_contiguous() and _native.token_major_ok(B, H, D, dout.dtype):
+            dattn = _ops.scatter_bwd_token_major(dout.transpose(1, 2).contiguous(), idx, S, S, L, p)
+        else:
+            dattn = _ops.scatter_bwd(dout.contiguous(), idx, S, S, L, p)
         dqs, dks, dvs = _ops.attn_bwd(qs, ks, vs, o, lse, dattn, scale)
         dxq, dxk, dxv = _ops.unpool_bwd(dqs, dks, dvs, inv, S, L, p)
         return dxq, dxk, dxv, None, None, None, None

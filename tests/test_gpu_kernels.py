@@ -209,3 +209,28 @@ def test_select_faster_than_reference_kernel(lh, O, cuda):
     print(f"\nselection at S=131072, k=2048, H=8: product {ours * 1e3:.1f} us, reference kernel + sort/gather "
           f"{ref * 1e3:.1f} us")
     assert ours < ref
+
+
+@pytest.mark.parametrize("shape", [(1, 16384, 8, 3, 4, 1024), (2, 8192, 2, 3, 2, 256)])
+def test_scatter_token_major_matches_head_major(lh, O, cuda, shape):
+    """The token-major fan-out (B, N, H, D) and its adjoint give the same values,
+    bit for bit, as the (B, H, N, D) kernels; the layer returns them as a
+    (B, H, S, D) view whose transpose the output projection reads for free."""
+    B, S, H, L, p, k = shape
+    D = 128
+    g = torch.Generator().manual_seed(9)
+    sq, sk = make_scores(B, H, S, L, p, "randn", 41)
+    idx, inv = lh._native.select_topk(sq.to(cuda), sk.to(cuda), L, p, k, S)
+    attn = torch.randn(B, H, idx.shape[-1], D, generator=g).to(torch.bfloat16).to(cuda)
+    ref = lh._native.scatter_fwd(attn, inv, S, S, L, p)
+    tm = lh._native.scatter_fwd_token_major(attn, inv, S, S, L, p)
+    assert tm.shape == (B, S, H, D) and torch.equal(tm.transpose(1, 2), ref)
+    dout = torch.randn(B, H, S, D, generator=g).to(torch.bfloat16).to(cuda)
+    assert torch.equal(lh._native.scatter_bwd_token_major(dout.transpose(1, 2).contiguous(), idx, S, S, L, p),
+                       lh._native.scatter_bwd(dout, idx, S, S, L, p))
+    xq, xk, xv = (torch.randn(B, S, H, D, generator=g).to(torch.bfloat16).to(cuda).requires_grad_(True)
+                  for _ in range(3))
+    out = lh.lighthouse_attention(xq, xk, xv, L, p, k)
+    assert out.shape == (B, H, S, D) and out.transpose(1, 2).is_contiguous()
+    out.transpose(1, 2).reshape(B, S, H * D).float().sum().backward()   # grad arrives token-major
+    assert all(torch.isfinite(t.grad).all() for t in (xq, xk, xv))

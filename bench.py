@@ -434,7 +434,8 @@ def run_model(args, rank, world, local_rank, cp=False):
 # every other point runs at S=98304, the reference's own seq_len, where all of
 # them are defined (the package raises LighthouseShapeError, as the reference
 # writes holes, on undefined shapes).
-SWEEP = [  # (S, L, p, k)
+SWEEP = [  # (S, L, p, k); the first point is BASELINE config 2
+    (65536, 3, 4, 2048),
     (131072, 3, 4, 2048), (131072, 3, 4, 4096),
     (98304, 3, 4, 1536), (98304, 3, 4, 2048), (98304, 3, 4, 3072), (98304, 3, 4, 4096), (98304, 3, 4, 6144),
     (98304, 3, 2, 1536), (98304, 4, 2, 1536), (98304, 5, 2, 1536),

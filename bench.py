@@ -15,7 +15,14 @@ all ranks' tokens / the max over ranks of the device time.
 ``--impl reference`` times the reference's CPU implementation of the path
 (the oracle's restatement: ATen scorer, C selection, torch.gather, CPU SDPA,
 index_add scatter -- the reference itself has no CPU selection or scatter)
-on the host cores, on rank 0 only, on a bounded sample of the same workload.
+on the host cores, on rank 0 only: the whole layer (all heads) per step, at
+most 3 timed steps after 1 warm-up (each step takes several seconds).
+
+The default line also carries, from the same run: every kernel group's time
+and HBM fraction (CUDA events inside the timed steps), the attention roofline
+against the measured bf16 peak (burst for a timed region under 2 s), the
+same-run cuDNN SDPA timing on the identical gathered tensors, the end-to-end
+figure through ``lighthouse_attention`` with host inputs, and the SM clocks.
 """
 from __future__ import annotations
 
